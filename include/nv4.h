@@ -1,0 +1,118 @@
+/*
+ * nv4 -- C ABI of the B200 (sm_100a) quantized-linear kernels of
+ * nano-vllm-int4: W4A4 activation prep (randomized Hadamard transform +
+ * per-128-group INT4 quantisation + packing), the grouped INT4 x INT4 GEMM with
+ * BF16 group scales, and the GPTQ W4A16 dequant GEMM.
+ *
+ * Conventions for every entry point:
+ *   - plain device pointers and sizes; no framework types;
+ *   - all buffers are caller-owned; nothing is retained across calls;
+ *   - work is enqueued on `stream` (a cudaStream_t passed as void*; NULL is the
+ *     legacy default stream) with no host synchronisation, no allocation and no
+ *     device-wide synchronisation, so every entry point may be captured in a
+ *     CUDA graph (the layer that calls them captures them at batch sizes 1..32);
+ *   - the return value is NV4_OK or a negative NV4_ERR_* code; nothing is
+ *     launched when an argument check fails.
+ * Tensors are dense row-major; "bf16" buffers hold IEEE bfloat16 bit patterns.
+ */
+#ifndef NV4_H_
+#define NV4_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NV4_OK 0
+#define NV4_ERR_INVALID_ARGUMENT (-1) /* shape, null pointer or flag out of range */
+#define NV4_ERR_UNSUPPORTED (-2)      /* valid request this build does not handle */
+#define NV4_ERR_ALIGNMENT (-3)        /* a pointer is not aligned as documented */
+#define NV4_ERR_CUDA (-4)             /* a CUDA runtime call failed (see nv4_last_cuda_error) */
+#define NV4_ERR_DEVICE (-5)           /* current device is not an sm_100 GPU */
+
+/* Activation layouts of nv4_rht_quant_pack. */
+#define NV4_LAYOUT_BLOCK128 0 /* normalized 128-point WHT per K group (TP-local) */
+#define NV4_LAYOUT_ROW_DH 1   /* row_DH_paley12_kron_sylvester_v1: H4096, or H12 (x) H1024 */
+
+/* Flags of nv4_w4a4_grouped_gemm. */
+#define NV4_GEMM_W_SCALE_GROUPED 1 /* w_scale is bf16 [N, K/128]; otherwise bf16 [N] */
+#define NV4_GEMM_OUT_FP32 2        /* out is float32 [M, N] (diagnostic); otherwise bf16 */
+#define NV4_GEMM_FORCE_STREAM 4    /* always use the weight-streaming mma.sync kernel (tests) */
+
+/*
+ * Randomized Hadamard transform, per-128-group activation quantisation and
+ * INT4 packing.  Replaces nanovllm/kernels/rht_a4_tilelang.py:150-163
+ * (rht_quant_pack) and its TileLang kernel (:19-136).
+ *
+ *   x          bf16 [m, k], 16-byte aligned
+ *   signs      int8 [k], values +-1, 8-byte aligned
+ *   out_packed int8 [m, k/2]: code of even k in the low nibble, 4-byte aligned
+ *   out_scale  bf16 [m, k/128]: BF16 group scale, rounded before the codes
+ *   layout     NV4_LAYOUT_BLOCK128 (k % 128 == 0) or NV4_LAYOUT_ROW_DH (k in {4096, 12288})
+ *   clamp_lo   -7 (reference checkpoint contract) or -8 (full signed INT4 range)
+ * code = round-half-even(x_rot / scale) clamped to [clamp_lo, 7]; an all-zero
+ * group has scale 1.0; the scale floor is the BF16 tiny.
+ */
+int nv4_rht_quant_pack(const void* x, const void* signs, void* out_packed, void* out_scale, int64_t m,
+                       int64_t k, int layout, int clamp_lo, void* stream);
+
+/*
+ * Grouped INT4 GEMM: out[m, n] = sum_g fp32-FMA(dot_g(a, w), sa[m,g] * sw[n,g]),
+ * groups of 128 along K in increasing g, one FP32 rounding per group, then BF16.
+ * Replaces nanovllm/kernels/w4a4_grouped_kernel.py:104-129 (w4a4_grouped_gemm)
+ * and, with NV4_GEMM_OUT_FP32, compile_grouped_gemm(..., output_fp32=True) (:31-91).
+ *
+ *   a_packed int8 [m, k/2] and w_packed int8 [n, k/2], 16-byte aligned rows (k % 32 == 0)
+ *   a_scale  bf16 [m, k/128]
+ *   w_scale  bf16 [n, k/128] with NV4_GEMM_W_SCALE_GROUPED, else bf16 [n]
+ *            (per-channel: out = (sum_g fp32-FMA(dot_g, sa[m,g])) * sw[n])
+ *   out      bf16 [m, n], or float32 with NV4_GEMM_OUT_FP32; every element is written
+ * Requirements: m, n >= 1, k % 128 == 0, n % 8 == 0.
+ */
+int nv4_w4a4_grouped_gemm(const void* a_packed, const void* w_packed, const void* a_scale, const void* w_scale,
+                          void* out, int64_t m, int64_t n, int64_t k, int flags, void* stream);
+
+/*
+ * Diagnostic: exact per-group INT32 dot products dots[g, m, n] of the same
+ * operands (the partials the GEMM scales and accumulates).  No reference
+ * counterpart is exported; the reference checks these partials through its
+ * FP32 diagnostic output (benchmarks/verify_w4a4_grouped.py:59-62).
+ */
+int nv4_w4a4_group_dots(const void* a_packed, const void* w_packed, int32_t* dots, int64_t m, int64_t n,
+                        int64_t k, void* stream);
+
+/*
+ * GPTQ W4A16 dequant GEMM: out[m, n] = x[m, k] @ W[k, n], with
+ * W[k, n] = bf16(bf16(w - z - 1) * bf16(scale[g, n])), g = k / group_size,
+ * FP32 accumulation, BF16 output.  Replaces nanovllm/layers/linear_w4a16.py:11-59
+ * (tl_dequant_matmul_w4a16); unlike the reference the caller's `out` need not
+ * be zeroed and the split-K partials are summed in FP32.
+ *
+ *   x        bf16 [m, k]
+ *   qweight  int32 [k/8, n]: nibble k%8 of k at bits 4*(k%8)
+ *   qzeros   int32 [k/group_size, n/8]: nibble n%8 at bits 4*(n%8)
+ *   scales   fp16 [k/group_size, n]
+ *   out      bf16 [m, n]
+ *   workspace   float32 scratch of nv4_w4a16_workspace_bytes(m, n, k) bytes
+ *               (may be NULL when that size is 0)
+ * Requirements: group_size == 128, k % 128 == 0, n % 64 == 0.
+ */
+int nv4_w4a16_gemm(const void* x, const void* qweight, const void* qzeros, const void* scales, void* out,
+                   int64_t m, int64_t n, int64_t k, int64_t group_size, void* workspace, int64_t workspace_bytes,
+                   void* stream);
+int64_t nv4_w4a16_workspace_bytes(int64_t m, int64_t n, int64_t k);
+
+/* Library metadata and error reporting. */
+int nv4_version(void);                      /* major*10000 + minor*100 + patch */
+const char* nv4_status_string(int status);  /* static string for a status code */
+int nv4_last_cuda_error(void);              /* cudaError_t of the last NV4_ERR_CUDA in this thread */
+/* Reads and clears the error word that bounded device-side waits set when they
+ * give up (0 = none).  Synchronises the current device. */
+int nv4_device_error(int* code);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NV4_H_ */

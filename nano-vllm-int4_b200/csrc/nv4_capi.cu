@@ -1,0 +1,209 @@
+// C ABI of libnv4 (declared in include/nv4.h): argument checks that mirror the
+// reference's Python validation, then dispatch to the kernel launchers.
+#include <cstdint>
+#include <mutex>
+
+#include "nv4_device.cuh"
+#include "nv4_launch.h"
+
+namespace nv4 {
+
+static thread_local int t_last_cuda_error = 0;
+void set_last_cuda_error(cudaError_t e) { t_last_cuda_error = static_cast<int>(e); }
+
+int current_device() {
+  int d = -1;
+  if (cudaGetDevice(&d) != cudaSuccess) return -1;
+  return d;
+}
+
+namespace {
+constexpr int kMaxDevices = 64;
+int g_sm_count[kMaxDevices] = {};
+int g_cc_major[kMaxDevices] = {};
+std::mutex g_mutex;
+
+int query_device(int dev) {
+  if (dev < 0 || dev >= kMaxDevices) return -1;
+  if (g_sm_count[dev] > 0) return dev;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (g_sm_count[dev] == 0) {
+    int sms = 0, major = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+      return -1;
+    g_cc_major[dev] = major;
+    g_sm_count[dev] = sms;
+  }
+  return dev;
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn g_encode = nullptr;
+
+EncodeTiledFn encode_fn() {
+  if (g_encode) return g_encode;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (!g_encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+  }
+  return g_encode;
+}
+}  // namespace
+
+int device_sm_count() {
+  const int dev = query_device(current_device());
+  return dev < 0 ? -1 : g_sm_count[dev];
+}
+
+static bool device_is_sm100() {
+  const int dev = query_device(current_device());
+  return dev >= 0 && g_cc_major[dev] == 10;
+}
+
+int ensure_smem_attr(const void* kernel, int bytes, int* done_flags) {
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices) return NV4_ERR_CUDA;
+  if (done_flags[dev] >= bytes) return NV4_OK;
+  const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return NV4_ERR_CUDA;
+  }
+  done_flags[dev] = bytes;
+  return NV4_OK;
+}
+
+bool make_tensor_map_u8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols_bytes, uint32_t box_rows,
+                        uint32_t box_cols_bytes, CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {cols_bytes, rows};
+  const cuuint64_t strides[1] = {cols_bytes};
+  const cuuint32_t box[2] = {box_cols_bytes, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int launch_w4a4_stream_gemm(const void* a_packed, const void* w_packed, const void* a_scale, const void* w_scale,
+                            void* out, int64_t m, int64_t n, int64_t k, int flags, cudaStream_t stream);
+
+int launch_w4a4_gemm(const void* a_packed, const void* w_packed, const void* a_scale, const void* w_scale, void* out,
+                     int64_t m, int64_t n, int64_t k, int flags, cudaStream_t stream) {
+  return launch_w4a4_stream_gemm(a_packed, w_packed, a_scale, w_scale, out, m, n, k, flags, stream);
+}
+
+}  // namespace nv4
+
+using namespace nv4;
+
+static inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+#pragma GCC visibility push(default)
+extern "C" {
+
+int nv4_version(void) { return 100; }  // 0.1.0
+
+const char* nv4_status_string(int status) {
+  switch (status) {
+    case NV4_OK: return "ok";
+    case NV4_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case NV4_ERR_UNSUPPORTED: return "unsupported configuration";
+    case NV4_ERR_ALIGNMENT: return "misaligned pointer";
+    case NV4_ERR_CUDA: return "CUDA runtime error";
+    case NV4_ERR_DEVICE: return "current device is not an sm_100 GPU";
+    default: return "unknown status";
+  }
+}
+
+int nv4_last_cuda_error(void) { return t_last_cuda_error; }
+
+int nv4_device_error(int* code) {
+  if (!code) return NV4_ERR_INVALID_ARGUMENT;
+  cudaError_t e = cudaDeviceSynchronize();
+  int v = 0;
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int));
+  const int zero = 0;
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return NV4_ERR_CUDA;
+  }
+  *code = v;
+  return NV4_OK;
+}
+
+int nv4_rht_quant_pack(const void* x, const void* signs, void* out_packed, void* out_scale, int64_t m, int64_t k,
+                       int layout, int clamp_lo, void* stream) {
+  if (!x || !signs || !out_packed || !out_scale || m < 1 || m > (int64_t(1) << 31) - 1)
+    return NV4_ERR_INVALID_ARGUMENT;
+  if (clamp_lo != -7 && clamp_lo != -8) return NV4_ERR_INVALID_ARGUMENT;
+  if (layout == NV4_LAYOUT_BLOCK128) {
+    if (k < 128 || k % 128 || k > (int64_t(1) << 24)) return NV4_ERR_INVALID_ARGUMENT;
+  } else if (layout == NV4_LAYOUT_ROW_DH) {
+    if (k != 4096 && k != 12288) return NV4_ERR_INVALID_ARGUMENT;
+  } else {
+    return NV4_ERR_INVALID_ARGUMENT;
+  }
+  if (!aligned(x, 16) || !aligned(signs, 8) || !aligned(out_packed, 4) || !aligned(out_scale, 2))
+    return NV4_ERR_ALIGNMENT;
+  if (!device_is_sm100()) return NV4_ERR_DEVICE;
+  return launch_rht_quant_pack(x, signs, out_packed, out_scale, m, k, layout, clamp_lo,
+                               static_cast<cudaStream_t>(stream));
+}
+
+int nv4_w4a4_grouped_gemm(const void* a_packed, const void* w_packed, const void* a_scale, const void* w_scale,
+                          void* out, int64_t m, int64_t n, int64_t k, int flags, void* stream) {
+  if (!a_packed || !w_packed || !a_scale || !w_scale || !out) return NV4_ERR_INVALID_ARGUMENT;
+  if (m < 1 || n < 1 || k < 128 || k % 128 || n % 8 || m > (int64_t(1) << 31) - 1 || n > (int64_t(1) << 31) - 1 ||
+      k > (int64_t(1) << 24))
+    return NV4_ERR_INVALID_ARGUMENT;
+  if (flags & ~(NV4_GEMM_W_SCALE_GROUPED | NV4_GEMM_OUT_FP32 | NV4_GEMM_FORCE_STREAM)) return NV4_ERR_INVALID_ARGUMENT;
+  if (!aligned(a_packed, 16) || !aligned(w_packed, 16) || !aligned(a_scale, 2) || !aligned(w_scale, 2) ||
+      !aligned(out, (flags & NV4_GEMM_OUT_FP32) ? 4 : 2))
+    return NV4_ERR_ALIGNMENT;
+  if (!device_is_sm100()) return NV4_ERR_DEVICE;
+  return launch_w4a4_gemm(a_packed, w_packed, a_scale, w_scale, out, m, n, k, flags,
+                          static_cast<cudaStream_t>(stream));
+}
+
+int nv4_w4a4_group_dots(const void* a_packed, const void* w_packed, int32_t* dots, int64_t m, int64_t n, int64_t k,
+                        void* stream) {
+  if (!a_packed || !w_packed || !dots || m < 1 || n < 1 || k < 128 || k % 128) return NV4_ERR_INVALID_ARGUMENT;
+  if ((k / 128) * m * n > (int64_t(1) << 31)) return NV4_ERR_UNSUPPORTED;
+  if (!aligned(dots, 4)) return NV4_ERR_ALIGNMENT;
+  if (!device_is_sm100()) return NV4_ERR_DEVICE;
+  return launch_w4a4_group_dots(a_packed, w_packed, dots, m, n, k, static_cast<cudaStream_t>(stream));
+}
+
+int64_t nv4_w4a16_workspace_bytes(int64_t m, int64_t n, int64_t k) {
+  if (m < 1 || n < 1 || k < 128) return 0;
+  return w4a16_workspace_bytes(m, n, k);
+}
+
+int nv4_w4a16_gemm(const void* x, const void* qweight, const void* qzeros, const void* scales, void* out, int64_t m,
+                   int64_t n, int64_t k, int64_t group_size, void* workspace, int64_t workspace_bytes, void* stream) {
+  if (!x || !qweight || !qzeros || !scales || !out) return NV4_ERR_INVALID_ARGUMENT;
+  if (group_size != 128) return NV4_ERR_UNSUPPORTED;
+  if (m < 1 || n < 64 || k < 128 || k % 128 || n % 64 || m > (int64_t(1) << 31) - 1 || k > (int64_t(1) << 24) ||
+      n > (int64_t(1) << 24))
+    return NV4_ERR_INVALID_ARGUMENT;
+  if (!aligned(x, 16) || !aligned(qweight, 4) || !aligned(qzeros, 4) || !aligned(scales, 2) || !aligned(out, 4) ||
+      (workspace && !aligned(workspace, 4)))
+    return NV4_ERR_ALIGNMENT;
+  if (!device_is_sm100()) return NV4_ERR_DEVICE;
+  return launch_w4a16_gemm(x, qweight, qzeros, scales, out, m, n, k, workspace, workspace_bytes,
+                           static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"
+#pragma GCC visibility pop

@@ -1,0 +1,65 @@
+// Host-side helpers shared by the kernel launchers (internal to libnv4).
+#pragma once
+
+#include <algorithm>
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "../../include/nv4.h"
+
+namespace nv4 {
+
+// Last failing cudaError_t of this host thread (reported by nv4_last_cuda_error).
+void set_last_cuda_error(cudaError_t e);
+
+int current_device();
+int device_sm_count();  // SMs of the current device (cached), <= 0 on failure
+
+// Launch `kernel` on `stream`.  With `pdl` the launch carries the programmatic
+// stream serialization attribute: the kernel may start while the previous
+// kernel in the stream is still running and must call griddepcontrol.wait
+// before reading that kernel's output.
+template <typename... KArgs, typename... Args>
+int launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
+                  Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  if (pdl) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return NV4_ERR_CUDA;
+  }
+  return NV4_OK;
+}
+
+// Opt a kernel into `bytes` of dynamic shared memory once per device.
+int ensure_smem_attr(const void* kernel, int bytes, int* done_flags /* [64] */);
+
+// 2-D tensor map over a row-major uint8 matrix [rows, cols_bytes] with a box of
+// [box_rows, box_cols_bytes] and the given swizzle; false on failure.
+bool make_tensor_map_u8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols_bytes, uint32_t box_rows,
+                        uint32_t box_cols_bytes, CUtensorMapSwizzle swizzle);
+
+// ---- launchers (one per kernel family) ----
+int launch_rht_quant_pack(const void* x, const void* signs, void* packed, void* scale, int64_t m, int64_t k,
+                          int layout, int clamp_lo, cudaStream_t stream);
+int launch_w4a4_gemm(const void* a_packed, const void* w_packed, const void* a_scale, const void* w_scale, void* out,
+                     int64_t m, int64_t n, int64_t k, int flags, cudaStream_t stream);
+int launch_w4a4_group_dots(const void* a_packed, const void* w_packed, int32_t* dots, int64_t m, int64_t n, int64_t k,
+                           cudaStream_t stream);
+int launch_w4a16_gemm(const void* x, const void* qweight, const void* qzeros, const void* scales, void* out,
+                      int64_t m, int64_t n, int64_t k, void* workspace, int64_t workspace_bytes, cudaStream_t stream);
+int64_t w4a16_workspace_bytes(int64_t m, int64_t n, int64_t k);
+
+}  // namespace nv4

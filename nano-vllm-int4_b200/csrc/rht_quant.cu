@@ -1,0 +1,432 @@
+// Kernel A: randomized Hadamard transform + per-128-group INT4 quantisation +
+// nibble packing, for the two activation layouts of the quantized-linear path.
+//
+//  * block128 (layout 0): a normalized 128-point Walsh-Hadamard transform of
+//    each K group after the sign multiply, with the arithmetic of the reference
+//    PyTorch path on CPU (benchmarks/rht_reference.py:26-39 fwht, then
+//    benchmarks/a4_group_quant.py:206-216 quantize_rotated): butterflies lowest
+//    index bit first, x / fl32(sqrt(128)) and scale = bf16(fl(fl(absmax*0.9)/7)),
+//    both IEEE divisions.
+//  * row_DH_paley12_kron_sylvester_v1 (layout 1): the reference checkpoint
+//    layout, with the arithmetic of nanovllm/kernels/rht_a4_tilelang.py:38-135:
+//    full-width H4096, or H1024 per factor followed by the Paley H12 mix summed
+//    source 0..11 and multiplied by fl32(1/sqrt(12)); scale uses
+//    __fmul_rn(__fmul_rn(absmax, 0.9f), fl32(1/7)).
+//
+// Both: scale rounded to BF16 before codes, 1.0 for an all-zero group, floor at
+// the BF16 tiny, code = round-half-even(__fdiv_rn(x, scale)) clamped to
+// [clamp_lo, 7], two codes per byte with the even K index in the low nibble.
+//
+// The butterflies map index bits to registers (3 low bits inside a 16-byte
+// load), to lanes (warp shuffles) and, for the full-width layout, to warps (one
+// shared-memory exchange); the FP32 result of every butterfly equals the
+// reference's because each output is the same single-rounded a+b or a-b.
+#include "nv4_device.cuh"
+#include "nv4_launch.h"
+
+namespace nv4 {
+
+constexpr unsigned kFull = 0xffffffffu;
+
+__device__ __forceinline__ float scale_block128(float mx) {
+  float t = __fmul_rn(mx, kClip);
+  float u = __fdiv_rn(t, 7.0f);
+  u = fmaxf(u, kBf16Tiny);
+  return (mx == 0.0f) ? 1.0f : u;
+}
+
+__device__ __forceinline__ float scale_rowdh(float mx) {
+  float t = __fmul_rn(mx, kClip);
+  t = __fmul_rn(t, kInv7);
+  t = fmaxf(t, kBf16Tiny);
+  return (mx == 0.0f) ? 1.0f : t;
+}
+
+// BF16-round the FP32 scale; returns the rounded value, bits in *bits.
+__device__ __forceinline__ float round_scale(float s, uint16_t* bits) {
+  __nv_bfloat16 b = __float2bfloat16_rn(s);
+  *bits = __bfloat16_as_ushort(b);
+  return __bfloat162float(b);
+}
+
+__device__ __forceinline__ uint32_t code_nibble(float v, float sf, int clamp_lo) {
+  int c = __float2int_rn(__fdiv_rn(v, sf));
+  c = max(c, clamp_lo);
+  c = min(c, 7);
+  return static_cast<uint32_t>(c) & 15u;
+}
+
+// Load 8 BF16 values (16 bytes) and apply 8 sign bits (bit e set = negate).
+__device__ __forceinline__ void load8_signed(const uint16_t* src, uint32_t sbits, float (&v)[8]) {
+  const uint4 w = __ldg(reinterpret_cast<const uint4*>(src));
+  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = __uint_as_float((ws[i] << 16) ^ (((sbits >> (2 * i)) & 1u) << 31));
+    v[2 * i + 1] = __uint_as_float((ws[i] & 0xFFFF0000u) ^ (((sbits >> (2 * i + 1)) & 1u) << 31));
+  }
+}
+
+// 8 sign bytes (int8 +-1) -> 8 bits, bit e set for a negative sign.
+__device__ __forceinline__ uint32_t sign_bits8(const int8_t* s) {
+  const uint2 w = *reinterpret_cast<const uint2*>(s);
+  uint32_t bits = 0;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) bits |= ((w.x >> (8 * e + 7)) & 1u) << e;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) bits |= ((w.y >> (8 * e + 7)) & 1u) << (e + 4);
+  return bits;
+}
+
+// Butterflies over index bits 0..2 held in registers (lowest bit first).
+__device__ __forceinline__ void butterfly8(float (&v)[8]) {
+#pragma unroll
+  for (int s = 1; s < 8; s <<= 1) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      if (!(e & s)) {
+        const float a = v[e], b = v[e + s];
+        v[e] = a + b;
+        v[e + s] = a - b;
+      }
+    }
+  }
+}
+
+// One butterfly stage across lanes (partner = lane ^ mask).  The lane holding
+// the low element computes a+b, the high one a-b; fma with +-1 rounds once.
+__device__ __forceinline__ float butterfly_lane(float v, int mask, bool high) {
+  const float other = __shfl_xor_sync(kFull, v, mask);
+  return fmaf(v, high ? -1.0f : 1.0f, other);
+}
+
+// ============================================================ block128
+struct Block128Args {
+  const uint16_t* x;
+  const int8_t* signs;
+  uint8_t* packed;
+  uint16_t* scale;
+  int M, K, G, ncb, warps_used, clamp_lo;
+};
+
+// A warp owns 8 consecutive groups (one "column block") of a row; lane q of
+// quad `quad` holds elements idx = j*32 + q*8 + e of group cb*8 + quad
+// (j: index bits 5-6, q: bits 3-4, e: bits 0-2).  Warps keep their column
+// block, and so their signs, while striding over rows.
+__global__ void __launch_bounds__(256) rht_block128_kernel(const Block128Args p) {
+  grid_dependents_launch();
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (gw >= p.warps_used) return;
+  const int cb = gw % p.ncb;
+  const int row_step = p.warps_used / p.ncb;
+  const int quad = lane >> 2, q = lane & 3;
+  const int g = cb * 8 + quad;
+  const bool active = g < p.G;
+  const bool hi1 = (q & 1) != 0, hi2 = (q & 2) != 0;
+
+  uint32_t sb[4] = {0, 0, 0, 0};
+  if (active) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) sb[j] = sign_bits8(p.signs + g * 128 + j * 32 + q * 8);
+  }
+  grid_dependency_wait();
+
+  for (int row = gw / p.ncb; row < p.M; row += row_step) {
+    float v[4][8];
+    if (active) {
+      const uint16_t* src = p.x + static_cast<size_t>(row) * p.K + g * 128 + q * 8;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) load8_signed(src + j * 32, sb[j], v[j]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[j][e] = 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) butterfly8(v[j]);                                  // bits 0-2
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[j][e] = butterfly_lane(v[j][e], 1, hi1);      // bit 3
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[j][e] = butterfly_lane(v[j][e], 2, hi2);      // bit 4
+#pragma unroll
+    for (int s = 1; s < 4; s <<= 1) {                                              // bits 5-6
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (!(j & s)) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float a = v[j][e], b = v[j + s][e];
+            v[j][e] = a + b;
+            v[j + s][e] = a - b;
+          }
+        }
+      }
+    }
+    float mx = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        v[j][e] = __fdiv_rn(v[j][e], kSqrt128);
+        mx = fmaxf(mx, fabsf(v[j][e]));
+      }
+    mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 2));
+    uint16_t sbits;
+    const float sf = round_scale(scale_block128(mx), &sbits);
+    if (active) {
+      uint8_t* dst = p.packed + static_cast<size_t>(row) * (p.K / 2) + g * 64 + q * 4;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) word |= code_nibble(v[j][e], sf, p.clamp_lo) << (4 * e);
+        *reinterpret_cast<uint32_t*>(dst + j * 16) = word;
+      }
+      if (q == 0) p.scale[static_cast<size_t>(row) * p.G + g] = sbits;
+    }
+  }
+}
+
+// ============================================================ row_DH
+struct RowDHArgs {
+  const uint16_t* x;
+  const int8_t* signs;
+  uint8_t* packed;
+  uint16_t* scale;
+  int M, clamp_lo;
+};
+
+// Shared-memory index with 4 floats of padding per 32 (keeps float4 accesses
+// of consecutive lanes on distinct banks).
+__host__ __device__ constexpr int padded(int k) { return k + ((k >> 5) << 2); }
+
+// Combine the four values at warp-index bits (b, b+1) into this warp's output
+// of two butterfly stages: stage b pairs (0,1),(2,3); stage b+1 pairs (0,2),(1,3).
+__device__ __forceinline__ float two_stages(float v0, float v1, float v2, float v3, int w) {
+  const float lo = (w & 1) ? v0 - v1 : v0 + v1;
+  const float hi = (w & 1) ? v2 - v3 : v2 + v3;
+  return (w & 2) ? lo - hi : lo + hi;
+}
+
+// K = 4096.  Thread (warp w, lane l) holds k = w*1024 + j*256 + l*8 + e:
+// e bits 0-2, lane bits 3-7, j bits 8-9, warp bits 10-11.
+__global__ void __launch_bounds__(128) rht_rowdh4096_kernel(const RowDHArgs p) {
+  grid_dependents_launch();
+  constexpr int K = 4096, G = 32;
+  __shared__ __align__(16) float sh[padded(K)];
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  uint32_t sb[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) sb[j] = sign_bits8(p.signs + w * 1024 + j * 256 + l * 8);
+  grid_dependency_wait();
+
+  for (int row = blockIdx.x; row < p.M; row += gridDim.x) {
+    float v[4][8];
+    const uint16_t* src = p.x + static_cast<size_t>(row) * K + w * 1024 + l * 8;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) load8_signed(src + j * 256, sb[j], v[j]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) butterfly8(v[j]);
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1)
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[j][e] = butterfly_lane(v[j][e], m, (l & m) != 0);
+#pragma unroll
+    for (int s = 1; s < 4; s <<= 1)
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (!(j & s)) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float a = v[j][e], b = v[j + s][e];
+            v[j][e] = a + b;
+            v[j + s][e] = a - b;
+          }
+        }
+    // warp bits 10-11 through shared memory
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float4* d = reinterpret_cast<float4*>(sh + padded(w * 1024 + j * 256 + l * 8));
+      d[0] = make_float4(v[j][0], v[j][1], v[j][2], v[j][3]);
+      d[1] = make_float4(v[j][4], v[j][5], v[j][6], v[j][7]);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float u[4][8];
+#pragma unroll
+      for (int ww = 0; ww < 4; ++ww) {
+        const float4* s4 = reinterpret_cast<const float4*>(sh + padded(ww * 1024 + j * 256 + l * 8));
+        const float4 a = s4[0], b = s4[1];
+        u[ww][0] = a.x; u[ww][1] = a.y; u[ww][2] = a.z; u[ww][3] = a.w;
+        u[ww][4] = b.x; u[ww][5] = b.y; u[ww][6] = b.z; u[ww][7] = b.w;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[j][e] = two_stages(u[0][e], u[1][e], u[2][e], u[3][e], w) * 0.015625f;
+    }
+    __syncthreads();
+    // groups: k >> 7 = w*8 + j*2 + (l >> 4); 16 lanes x 8 values each
+    uint8_t* dst = p.packed + static_cast<size_t>(row) * (K / 2) + (w * 1024 + l * 8) / 2;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float mx = 0.0f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) mx = fmaxf(mx, fabsf(v[j][e]));
+#pragma unroll
+      for (int m = 1; m < 16; m <<= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, m));
+      uint16_t sbits;
+      const float sf = round_scale(scale_rowdh(mx), &sbits);
+      uint32_t word = 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) word |= code_nibble(v[j][e], sf, p.clamp_lo) << (4 * e);
+      *reinterpret_cast<uint32_t*>(dst + j * 128) = word;
+      if ((l & 15) == 0) p.scale[static_cast<size_t>(row) * G + w * 8 + j * 2 + (l >> 4)] = sbits;
+    }
+  }
+}
+
+__device__ __forceinline__ bool h12_positive(int source, int destination) {
+  if (source == 0 || destination == 0) return true;
+  const int d = (destination - source + 11) % 11;
+  return d == 1 || d == 3 || d == 4 || d == 5 || d == 9;
+}
+
+// K = 12288 = 12 x 1024.  Thread (warp w, lane l) holds, for each factor f,
+// k = f*1024 + w*256 + l*8 + e: e bits 0-2, lane bits 3-7, warp bits 8-9 of
+// the 1024-point transform; the 12 factors of a position live in one thread,
+// so the H12 mix is register-local.
+__global__ void __launch_bounds__(128) rht_rowdh12288_kernel(const RowDHArgs p) {
+  grid_dependents_launch();
+  constexpr int K = 12288, G = 96;
+  extern __shared__ __align__(16) float shd[];
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  uint32_t sb[12];
+#pragma unroll
+  for (int f = 0; f < 12; ++f) sb[f] = sign_bits8(p.signs + f * 1024 + w * 256 + l * 8);
+  grid_dependency_wait();
+
+  for (int row = blockIdx.x; row < p.M; row += gridDim.x) {
+    float v[12][8];
+    const uint16_t* src = p.x + static_cast<size_t>(row) * K + w * 256 + l * 8;
+#pragma unroll
+    for (int f = 0; f < 12; ++f) load8_signed(src + f * 1024, sb[f], v[f]);
+#pragma unroll
+    for (int f = 0; f < 12; ++f) butterfly8(v[f]);
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1)
+#pragma unroll
+      for (int f = 0; f < 12; ++f)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[f][e] = butterfly_lane(v[f][e], m, (l & m) != 0);
+#pragma unroll
+    for (int f = 0; f < 12; ++f) {
+      float4* d = reinterpret_cast<float4*>(shd + padded(f * 1024 + w * 256 + l * 8));
+      d[0] = make_float4(v[f][0], v[f][1], v[f][2], v[f][3]);
+      d[1] = make_float4(v[f][4], v[f][5], v[f][6], v[f][7]);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int f = 0; f < 12; ++f) {
+      float u[4][8];
+#pragma unroll
+      for (int ww = 0; ww < 4; ++ww) {
+        const float4* s4 = reinterpret_cast<const float4*>(shd + padded(f * 1024 + ww * 256 + l * 8));
+        const float4 a = s4[0], b = s4[1];
+        u[ww][0] = a.x; u[ww][1] = a.y; u[ww][2] = a.z; u[ww][3] = a.w;
+        u[ww][4] = b.x; u[ww][5] = b.y; u[ww][6] = b.z; u[ww][7] = b.w;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[f][e] = two_stages(u[0][e], u[1][e], u[2][e], u[3][e], w) * 0.03125f;
+    }
+    __syncthreads();
+    // Paley H12 across the factors: out[d] = sum_s H12[s,d] z[s], s = 0..11.
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float b[12];
+#pragma unroll
+      for (int d = 0; d < 12; ++d) {
+        float acc = 0.0f;
+#pragma unroll
+        for (int s = 0; s < 12; ++s) acc = h12_positive(s, d) ? acc + v[s][e] : acc - v[s][e];
+        b[d] = acc * kInvSqrt12;
+      }
+#pragma unroll
+      for (int d = 0; d < 12; ++d) v[d][e] = b[d];
+    }
+    uint8_t* dst = p.packed + static_cast<size_t>(row) * (K / 2) + (w * 256 + l * 8) / 2;
+#pragma unroll
+    for (int f = 0; f < 12; ++f) {
+      float mx = 0.0f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) mx = fmaxf(mx, fabsf(v[f][e]));
+#pragma unroll
+      for (int m = 1; m < 16; m <<= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, m));
+      uint16_t sbits;
+      const float sf = round_scale(scale_rowdh(mx), &sbits);
+      uint32_t word = 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) word |= code_nibble(v[f][e], sf, p.clamp_lo) << (4 * e);
+      *reinterpret_cast<uint32_t*>(dst + f * 512) = word;
+      if ((l & 15) == 0) p.scale[static_cast<size_t>(row) * G + f * 8 + w * 2 + (l >> 4)] = sbits;
+    }
+  }
+}
+
+// ============================================================ host launchers
+constexpr int kRowDH12288Smem = padded(12288) * 4;
+
+int launch_rht_quant_pack(const void* x, const void* signs, void* packed, void* scale, int64_t m, int64_t k,
+                          int layout, int clamp_lo, cudaStream_t stream) {
+  const int sms = device_sm_count();
+  if (sms <= 0) return NV4_ERR_CUDA;
+  if (layout == NV4_LAYOUT_BLOCK128) {
+    Block128Args a;
+    a.x = static_cast<const uint16_t*>(x);
+    a.signs = static_cast<const int8_t*>(signs);
+    a.packed = static_cast<uint8_t*>(packed);
+    a.scale = static_cast<uint16_t*>(scale);
+    a.M = static_cast<int>(m);
+    a.K = static_cast<int>(k);
+    a.G = static_cast<int>(k / 128);
+    a.ncb = (a.G + 7) / 8;
+    a.clamp_lo = clamp_lo;
+    const int64_t tasks = m * a.ncb;
+    int64_t warps = std::min<int64_t>(tasks, static_cast<int64_t>(sms) * 32);
+    warps = std::max<int64_t>(a.ncb, (warps / a.ncb) * a.ncb);
+    a.warps_used = static_cast<int>(warps);
+    const int blocks = static_cast<int>((warps + 7) / 8);
+    return launch_kernel(rht_block128_kernel, dim3(blocks), dim3(256), 0, stream, false, a);
+  }
+  RowDHArgs a;
+  a.x = static_cast<const uint16_t*>(x);
+  a.signs = static_cast<const int8_t*>(signs);
+  a.packed = static_cast<uint8_t*>(packed);
+  a.scale = static_cast<uint16_t*>(scale);
+  a.M = static_cast<int>(m);
+  a.clamp_lo = clamp_lo;
+  if (k == 4096) {
+    const int blocks = static_cast<int>(std::min<int64_t>(m, static_cast<int64_t>(sms) * 8));
+    return launch_kernel(rht_rowdh4096_kernel, dim3(blocks), dim3(128), 0, stream, false, a);
+  }
+  static bool attr_set[64] = {};
+  const int dev = current_device();
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    if (cudaFuncSetAttribute(rht_rowdh12288_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kRowDH12288Smem) != cudaSuccess)
+      return NV4_ERR_CUDA;
+    attr_set[dev] = true;
+  }
+  const int blocks = static_cast<int>(std::min<int64_t>(m, static_cast<int64_t>(sms) * 4));
+  return launch_kernel(rht_rowdh12288_kernel, dim3(blocks), dim3(128), kRowDH12288Smem, stream, false, a);
+}
+
+}  // namespace nv4

@@ -1,0 +1,150 @@
+"""ctypes binding of libnv4.so, the sm_100a kernel library (C ABI in include/nv4.h).
+
+This is the only route from Python to the kernels.  There is no fallback: if
+the library is missing, or the current device is not an sm_100 GPU, every
+entry point raises.  Tensors are passed as raw device pointers and the work is
+enqueued on torch's current stream of the tensors' device, so calls compose
+with torch's stream semantics and CUDA-graph capture.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libnv4.so")
+
+OK = 0
+ERR_INVALID_ARGUMENT = -1
+ERR_UNSUPPORTED = -2
+ERR_ALIGNMENT = -3
+ERR_CUDA = -4
+ERR_DEVICE = -5
+
+LAYOUT_BLOCK128 = 0
+LAYOUT_ROW_DH = 1
+LAYOUTS = {"block128": LAYOUT_BLOCK128, "row_DH_paley12_kron_sylvester_v1": LAYOUT_ROW_DH,
+           "row_dh": LAYOUT_ROW_DH, "row_DH": LAYOUT_ROW_DH}
+
+GEMM_W_SCALE_GROUPED = 1
+GEMM_OUT_FP32 = 2
+GEMM_FORCE_STREAM = 4
+
+EXPORTS = ("nv4_rht_quant_pack", "nv4_w4a4_grouped_gemm", "nv4_w4a4_group_dots", "nv4_w4a16_gemm",
+           "nv4_w4a16_workspace_bytes", "nv4_version", "nv4_status_string", "nv4_last_cuda_error",
+           "nv4_device_error")
+
+
+class NativeLibraryError(RuntimeError):
+    """libnv4.so is missing or failed to load."""
+
+
+class NativeCallError(RuntimeError):
+    """A libnv4 entry point returned an error status."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(message)
+        self.status = status
+
+
+_lib = None
+_lock = threading.Lock()
+_vp, _i64, _int = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+
+
+def load(path: str | None = None) -> ctypes.CDLL:
+    """Load libnv4.so once (raises NativeLibraryError when it is absent)."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    with _lock:
+        if _lib is not None and path is None:
+            return _lib
+        p = path or LIB_PATH
+        if not os.path.exists(p):
+            raise NativeLibraryError(
+                f"libnv4.so not found at {p}; build it with `python nano-vllm-int4_b200/build_native.py`")
+        try:
+            lib = ctypes.CDLL(p)
+        except OSError as e:  # pragma: no cover - depends on the host
+            raise NativeLibraryError(f"failed to load {p}: {e}") from e
+        lib.nv4_rht_quant_pack.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _int, _int, _vp]
+        lib.nv4_w4a4_grouped_gemm.argtypes = [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]
+        lib.nv4_w4a4_group_dots.argtypes = [_vp, _vp, _vp, _i64, _i64, _i64, _vp]
+        lib.nv4_w4a16_gemm.argtypes = [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _vp]
+        lib.nv4_w4a16_workspace_bytes.argtypes = [_i64, _i64, _i64]
+        lib.nv4_w4a16_workspace_bytes.restype = _i64
+        lib.nv4_status_string.argtypes = [_int]
+        lib.nv4_status_string.restype = ctypes.c_char_p
+        lib.nv4_device_error.argtypes = [ctypes.POINTER(_int)]
+        for name in ("nv4_rht_quant_pack", "nv4_w4a4_grouped_gemm", "nv4_w4a4_group_dots", "nv4_w4a16_gemm",
+                     "nv4_version", "nv4_last_cuda_error", "nv4_device_error"):
+            getattr(lib, name).restype = _int
+        if path is None:
+            _lib = lib
+        return lib
+
+
+def check(status: int, what: str) -> None:
+    if status == OK:
+        return
+    lib = load()
+    text = lib.nv4_status_string(status).decode()
+    if status == ERR_CUDA:
+        text += f" (cudaError {lib.nv4_last_cuda_error()})"
+    if status in (ERR_INVALID_ARGUMENT, ERR_ALIGNMENT, ERR_UNSUPPORTED):
+        raise ValueError(f"{what}: {text}")
+    raise NativeCallError(status, f"{what}: {text}")
+
+
+def ptr(t: torch.Tensor) -> ctypes.c_void_p:
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def stream_of(t: torch.Tensor) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def device_error() -> int:
+    """Read and clear the error word of the current device (synchronises)."""
+    code = _int(0)
+    check(load().nv4_device_error(ctypes.byref(code)), "nv4_device_error")
+    return code.value
+
+
+def rht_quant_pack(x, signs, packed, scale, layout: int, clamp_lo: int) -> None:
+    m, k = x.shape
+    with torch.cuda.device(x.device):
+        check(load().nv4_rht_quant_pack(ptr(x), ptr(signs), ptr(packed), ptr(scale), m, k, layout, clamp_lo,
+                                        stream_of(x)), "nv4_rht_quant_pack")
+
+
+def w4a4_grouped_gemm(a_packed, w_packed, a_scale, w_scale, out, flags: int) -> None:
+    m, n, k = a_packed.shape[0], w_packed.shape[0], a_packed.shape[1] * 2
+    with torch.cuda.device(a_packed.device):
+        check(load().nv4_w4a4_grouped_gemm(ptr(a_packed), ptr(w_packed), ptr(a_scale), ptr(w_scale), ptr(out),
+                                           m, n, k, flags, stream_of(a_packed)), "nv4_w4a4_grouped_gemm")
+
+
+def w4a4_group_dots(a_packed, w_packed, dots) -> None:
+    m, n, k = a_packed.shape[0], w_packed.shape[0], a_packed.shape[1] * 2
+    with torch.cuda.device(a_packed.device):
+        check(load().nv4_w4a4_group_dots(ptr(a_packed), ptr(w_packed), ptr(dots), m, n, k, stream_of(a_packed)),
+              "nv4_w4a4_group_dots")
+
+
+def w4a16_workspace_bytes(m: int, n: int, k: int, device) -> int:
+    with torch.cuda.device(device):
+        return int(load().nv4_w4a16_workspace_bytes(m, n, k))
+
+
+def w4a16_gemm(x, qweight, qzeros, scales, out, group_size: int, workspace) -> None:
+    m, k = x.shape
+    n = qweight.shape[1]
+    ws_ptr = ptr(workspace) if workspace is not None else ctypes.c_void_p(0)
+    ws_bytes = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    with torch.cuda.device(x.device):
+        check(load().nv4_w4a16_gemm(ptr(x), ptr(qweight), ptr(qzeros), ptr(scales), ptr(out), m, n, k, group_size,
+                                    ws_ptr, ws_bytes, stream_of(x)), "nv4_w4a16_gemm")

@@ -1,0 +1,92 @@
+"""Activation prep for W4A4: RHT + per-128-group INT4 quantisation + packing.
+
+Drop-in for ``nanovllm/kernels/rht_a4_tilelang.py`` of the reference (the
+module name is kept so that callers and the reference's plugin harness
+``bench_rht_a4.py --impl nanovllm.kernels.rht_a4_tilelang:rht_quant_pack`` need
+no change); the implementation is the sm_100a CUDA kernel in libnv4.
+
+``rht_quant_pack(x, signs, *, out_packed, out_scale)`` keeps the reference
+contract (``benchmarks/rht_a4_bench_common.py:276-293``): layout
+``row_DH_paley12_kron_sylvester_v1``, clip 0.9, BF16 scale rounded before the
+codes, codes in [-7, 7], outputs written in place and returned, current CUDA
+stream, no host synchronisation, CUDA-graph safe.  Two keyword-only extensions
+select the other layout and code range used by the benchmark configurations:
+``layout="block128"`` (normalized 128-point WHT per K group, any K % 128 == 0)
+and ``clamp_lo=-8``.
+"""
+from dataclasses import dataclass
+from functools import lru_cache
+
+import torch
+
+from nanovllm import _native
+
+LAYOUT_VERSION = "row_DH_paley12_kron_sylvester_v1"
+
+
+@dataclass(frozen=True)
+class Config:
+    """Kept for API compatibility (rht_a4_tilelang.py:13-16).  The CUDA kernel
+    chooses its own geometry; these fields are validated and otherwise unused."""
+    threads_per_row: int = 128
+    rows_per_block: int = 1
+
+
+def _check_config(cfg: Config) -> None:
+    if cfg.threads_per_row not in (32, 64, 128, 256, 512) or cfg.rows_per_block < 1 \
+            or cfg.threads_per_row * cfg.rows_per_block > 1024:
+        raise ValueError("Unsupported RHT configuration")
+
+
+@lru_cache(None)
+def compile_kernel(K, cfg=Config()):
+    """Returns a launcher ``fn(x, signs, packed, scale)`` for the reference layout
+    (rht_a4_tilelang.py:19-136 compiled a TileLang kernel here)."""
+    if K not in (4096, 12288):
+        raise ValueError("Unsupported RHT configuration")
+    _check_config(cfg)
+
+    def launch(x, signs, packed, scale):
+        _native.rht_quant_pack(x, signs, packed, scale, _native.LAYOUT_ROW_DH, -7)
+    return launch
+
+
+@lru_cache(None)
+def best_config(M, K):
+    return Config()
+
+
+def _layout_id(layout) -> int:
+    if isinstance(layout, int):
+        if layout not in (_native.LAYOUT_BLOCK128, _native.LAYOUT_ROW_DH):
+            raise ValueError(f"unknown layout {layout}")
+        return layout
+    try:
+        return _native.LAYOUTS[layout]
+    except KeyError:
+        raise ValueError(f"unknown layout {layout!r}") from None
+
+
+def rht_quant_pack(x, signs, *, out_packed, out_scale, config=None, layout=LAYOUT_VERSION, clamp_lo=-7):
+    lid = _layout_id(layout)
+    if x.ndim != 2 or x.dtype != torch.bfloat16 or x.shape[0] < 1:
+        raise ValueError('Expected BF16 X[M,K], M>0, K=4096/12288')
+    m, k = x.shape
+    if lid == _native.LAYOUT_ROW_DH and k not in (4096, 12288):
+        raise ValueError('Expected BF16 X[M,K], M>0, K=4096/12288')
+    if lid == _native.LAYOUT_BLOCK128 and (k < 128 or k % 128):
+        raise ValueError('Expected BF16 X[M,K], M>0, K a multiple of 128 for the block128 layout')
+    if signs.shape != (k,) or signs.dtype != torch.int8:
+        raise ValueError('Expected INT8 signs[K]')
+    if out_packed.shape != (m, k // 2) or out_packed.dtype != torch.int8:
+        raise ValueError('Expected INT8 output[M,K/2]')
+    if out_scale.shape != (m, k // 128) or out_scale.dtype != torch.bfloat16:
+        raise ValueError('Expected BF16 scales[M,K/128]')
+    if any(not t.is_cuda or not t.is_contiguous() or t.device != x.device for t in [x, signs, out_packed, out_scale]):
+        raise ValueError('All tensors must be contiguous on one CUDA device')
+    if clamp_lo not in (-7, -8):
+        raise ValueError('clamp_lo must be -7 or -8')
+    if config is not None:
+        _check_config(config)
+    _native.rht_quant_pack(x, signs, out_packed, out_scale, lid, clamp_lo)
+    return out_packed, out_scale

@@ -1,0 +1,231 @@
+"""W4A4 linear layers: activation prep (RHT + INT4 quantisation) + grouped INT4 GEMM.
+
+``W4A4Linear`` is the drop-in for ``nanovllm/layers/linear_w4a4.py:15-36`` of
+the reference: same constructor, buffer names, dtypes and shapes
+(``packed_weight`` int8 [N, K/2], ``weight_scale`` bf16 [N, K/128], ``signs``
+int8 [K]), same forward (two launches, two small allocations that come from
+the CUDA-graph pool when captured).  Its defaults reproduce the reference
+checkpoint contract (layout ``row_DH_paley12_kron_sylvester_v1``, codes in
+[-7, 7]); ``layout="block128", clamp_lo=-8`` selects the block-diagonal layout
+and full INT4 range of the benchmark configurations.
+
+Tensor parallelism is new relative to the reference (which refuses it for
+W4A4, ``linear_w4a4.py:18-19``).  The classes below follow the BF16 pattern of
+``nanovllm/layers/linear.py:54-155``:
+
+* ``W4A4ColumnParallelLinear`` / ``W4A4MergedColumnParallelLinear`` /
+  ``W4A4QKVParallelLinear`` shard the output dimension N.  Every rank holds the
+  full sign vector and quantises the (replicated) input itself; no
+  communication.
+* ``W4A4RowParallelLinear`` shards K on 128-group boundaries.  With the
+  ``block128`` layout the transform and quantisation of a K shard need only
+  that shard, so each rank runs the GEMM on its groups into FP32 and the
+  partial outputs are summed with one all-reduce over NVLink (NCCL).  The
+  full-width checkpoint layout mixes all of K, so row-parallel ranks first
+  all-gather the BF16 input, quantise the whole row and keep their groups.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+from torch import nn
+
+from nanovllm.kernels.rht_a4_tilelang import LAYOUT_VERSION, rht_quant_pack
+from nanovllm.kernels.w4a4_grouped_kernel import w4a4_grouped_gemm
+from nanovllm import _native
+
+BLOCK128 = "block128"
+
+
+def _tp(tp_rank, tp_size):
+    if tp_size is None:
+        tp_size = dist.get_world_size() if dist.is_initialized() else 1
+    if tp_rank is None:
+        tp_rank = dist.get_rank() if dist.is_initialized() else 0
+    return tp_rank, tp_size
+
+
+def _divide(numerator, denominator):
+    if numerator % denominator:
+        raise ValueError(f"{numerator} is not divisible by {denominator}")
+    return numerator // denominator
+
+
+class W4A4Linear(nn.Module):
+    def __init__(self, input_size: int, output_size: int, bias: bool = False, *, layout=LAYOUT_VERSION,
+                 clamp_lo: int = -7):
+        super().__init__()
+        if type(self) is W4A4Linear and dist.is_initialized() and dist.get_world_size() != 1:
+            raise ValueError("W4A4Linear supports one GPU only; use the W4A4*ParallelLinear classes")
+        self.layout_id = _native.LAYOUTS[layout] if isinstance(layout, str) else int(layout)
+        if bias or output_size % 8:
+            raise ValueError("W4A4 requires bias-free Qwen3-8B projection shapes")
+        if self.layout_id == _native.LAYOUT_ROW_DH and input_size not in (4096, 12288):
+            raise ValueError("W4A4 requires bias-free Qwen3-8B projection shapes")
+        if input_size % 128:
+            raise ValueError("W4A4 requires K divisible by 128")
+        if clamp_lo not in (-7, -8):
+            raise ValueError("clamp_lo must be -7 or -8")
+        self.layout = layout
+        self.clamp_lo = clamp_lo
+        self.in_features, self.out_features = input_size, output_size
+        self.register_buffer("packed_weight", torch.empty(output_size, input_size // 2, dtype=torch.int8))
+        self.register_buffer("weight_scale", torch.empty(output_size, input_size // 128, dtype=torch.bfloat16))
+        self.register_buffer("signs", torch.empty(input_size, dtype=torch.int8))
+
+    def quantize_input(self, flat: torch.Tensor):
+        m, k = flat.shape
+        packed = torch.empty((m, k // 2), dtype=torch.int8, device=flat.device)
+        scale = torch.empty((m, k // 128), dtype=torch.bfloat16, device=flat.device)
+        rht_quant_pack(flat, self.signs, out_packed=packed, out_scale=scale, layout=self.layout_id,
+                       clamp_lo=self.clamp_lo)
+        return packed, scale
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if x.shape[-1] != self.in_features or x.dtype != torch.bfloat16:
+            raise ValueError("W4A4Linear requires BF16 activations with the configured input width")
+        flat = x.reshape(-1, self.in_features).contiguous()
+        packed, scale = self.quantize_input(flat)
+        out = w4a4_grouped_gemm(packed, self.packed_weight, scale, self.weight_scale)
+        return out.reshape(*x.shape[:-1], self.out_features)
+
+    @torch.no_grad()
+    def load_full(self, packed: torch.Tensor, scale: torch.Tensor, signs: torch.Tensor) -> None:
+        """Copy unsharded checkpoint tensors (packed [N,K/2], scale [N,K/128], signs [K])."""
+        self.packed_weight.copy_(packed)
+        self.weight_scale.copy_(scale)
+        self.signs.copy_(signs)
+
+
+class W4A4ColumnParallelLinear(W4A4Linear):
+    """Output dimension sharded over the TP group (linear.py:54-73 pattern)."""
+
+    def __init__(self, input_size: int, output_size: int, bias: bool = False, *, layout=BLOCK128,
+                 clamp_lo: int = -8, tp_rank=None, tp_size=None):
+        self.tp_rank, self.tp_size = _tp(tp_rank, tp_size)
+        self.full_output_size = output_size
+        super().__init__(input_size, _divide(output_size, self.tp_size), bias, layout=layout, clamp_lo=clamp_lo)
+
+    def _rows(self, full_rows: int):
+        size = _divide(full_rows, self.tp_size)
+        return self.tp_rank * size, size
+
+    @torch.no_grad()
+    def load_full(self, packed, scale, signs):
+        start, size = self._rows(packed.shape[0])
+        self.packed_weight.copy_(packed.narrow(0, start, size))
+        self.weight_scale.copy_(scale.narrow(0, start, size))
+        self.signs.copy_(signs)
+
+
+class W4A4MergedColumnParallelLinear(W4A4ColumnParallelLinear):
+    """Several column blocks (e.g. gate and up) concatenated along N, each sharded
+    separately so that every rank holds matching slices (linear.py:76-93)."""
+
+    def __init__(self, input_size: int, output_sizes: list[int], bias: bool = False, **kw):
+        self.output_sizes = list(output_sizes)
+        super().__init__(input_size, sum(output_sizes), bias, **kw)
+
+    @torch.no_grad()
+    def load_shard(self, shard_id: int, packed, scale):
+        offset = sum(self.output_sizes[:shard_id]) // self.tp_size
+        size = self.output_sizes[shard_id] // self.tp_size
+        self.packed_weight.narrow(0, offset, size).copy_(packed.chunk(self.tp_size, 0)[self.tp_rank])
+        self.weight_scale.narrow(0, offset, size).copy_(scale.chunk(self.tp_size, 0)[self.tp_rank])
+
+    @torch.no_grad()
+    def load_full(self, packed, scale, signs):
+        start = 0
+        for i, n in enumerate(self.output_sizes):
+            self.load_shard(i, packed.narrow(0, start, n), scale.narrow(0, start, n))
+            start += n
+        self.signs.copy_(signs)
+
+
+class W4A4QKVParallelLinear(W4A4ColumnParallelLinear):
+    """Fused q/k/v projection sharded by heads (linear.py:96-128)."""
+
+    def __init__(self, hidden_size: int, head_size: int, total_num_heads: int, total_num_kv_heads=None,
+                 bias: bool = False, **kw):
+        tp_rank, tp_size = _tp(kw.get("tp_rank"), kw.get("tp_size"))
+        total_num_kv_heads = total_num_kv_heads or total_num_heads
+        self.head_size = head_size
+        self.total_num_heads, self.total_num_kv_heads = total_num_heads, total_num_kv_heads
+        self.num_heads = _divide(total_num_heads, tp_size)
+        self.num_kv_heads = _divide(total_num_kv_heads, tp_size)
+        super().__init__(hidden_size, (total_num_heads + 2 * total_num_kv_heads) * head_size, bias, **kw)
+
+    @torch.no_grad()
+    def load_shard(self, shard_id: str, packed, scale):
+        if shard_id not in ("q", "k", "v"):
+            raise ValueError(shard_id)
+        q = self.num_heads * self.head_size
+        kv = self.num_kv_heads * self.head_size
+        offset, size = {"q": (0, q), "k": (q, kv), "v": (q + kv, kv)}[shard_id]
+        self.packed_weight.narrow(0, offset, size).copy_(packed.chunk(self.tp_size, 0)[self.tp_rank])
+        self.weight_scale.narrow(0, offset, size).copy_(scale.chunk(self.tp_size, 0)[self.tp_rank])
+
+    @torch.no_grad()
+    def load_full(self, packed, scale, signs):
+        q = self.total_num_heads * self.head_size
+        kv = self.total_num_kv_heads * self.head_size
+        for sid, (start, n) in zip("qkv", ((0, q), (q, kv), (q + kv, kv))):
+            self.load_shard(sid, packed.narrow(0, start, n), scale.narrow(0, start, n))
+        self.signs.copy_(signs)
+
+
+class W4A4RowParallelLinear(W4A4Linear):
+    """Input dimension K sharded on 128-group boundaries; partial outputs summed
+    in FP32 with one all-reduce (linear.py:131-155 pattern)."""
+
+    def __init__(self, input_size: int, output_size: int, bias: bool = False, *, layout=BLOCK128,
+                 clamp_lo: int = -8, tp_rank=None, tp_size=None, group=None):
+        self.tp_rank, self.tp_size = _tp(tp_rank, tp_size)
+        self.group = group
+        self.full_input_size = input_size
+        k_local = _divide(input_size, self.tp_size)
+        if k_local % 128:
+            raise ValueError("row-parallel K shards must be whole 128-groups")
+        lid = _native.LAYOUTS[layout] if isinstance(layout, str) else int(layout)
+        self.gather_input = lid == _native.LAYOUT_ROW_DH and self.tp_size > 1
+        # With the full-width layout the module quantises the gathered row, so its
+        # signs buffer covers all of K; the weights cover this rank's K shard.
+        nn.Module.__init__(self)
+        self.layout, self.layout_id, self.clamp_lo = layout, lid, clamp_lo
+        if bias or output_size % 8 or clamp_lo not in (-7, -8):
+            raise ValueError("W4A4 requires bias-free projection shapes")
+        if lid == _native.LAYOUT_ROW_DH and input_size not in (4096, 12288):
+            raise ValueError("W4A4 requires bias-free Qwen3-8B projection shapes")
+        self.in_features, self.out_features = k_local, output_size
+        self.register_buffer("packed_weight", torch.empty(output_size, k_local // 2, dtype=torch.int8))
+        self.register_buffer("weight_scale", torch.empty(output_size, k_local // 128, dtype=torch.bfloat16))
+        self.register_buffer("signs", torch.empty(input_size if self.gather_input else k_local, dtype=torch.int8))
+
+    @torch.no_grad()
+    def load_full(self, packed, scale, signs):
+        k_local = self.in_features
+        self.packed_weight.copy_(packed.narrow(1, self.tp_rank * k_local // 2, k_local // 2))
+        self.weight_scale.copy_(scale.narrow(1, self.tp_rank * k_local // 128, k_local // 128))
+        self.signs.copy_(signs if self.gather_input else signs.narrow(0, self.tp_rank * k_local, k_local))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if x.shape[-1] != self.in_features or x.dtype != torch.bfloat16:
+            raise ValueError("W4A4RowParallelLinear requires BF16 activations of the local K shard")
+        flat = x.reshape(-1, self.in_features).contiguous()
+        if self.gather_input:
+            parts = [torch.empty_like(flat) for _ in range(self.tp_size)]
+            dist.all_gather(parts, flat, group=self.group)
+            full = torch.cat(parts, dim=1)
+            packed_full, scale_full = W4A4Linear.quantize_input(self, full)
+            k_local = self.in_features
+            packed = packed_full[:, self.tp_rank * k_local // 2:(self.tp_rank + 1) * k_local // 2].contiguous()
+            scale = scale_full[:, self.tp_rank * k_local // 128:(self.tp_rank + 1) * k_local // 128].contiguous()
+        else:
+            packed, scale = self.quantize_input(flat)
+        if self.tp_size == 1:
+            out = w4a4_grouped_gemm(packed, self.packed_weight, scale, self.weight_scale)
+        else:
+            partial = w4a4_grouped_gemm(packed, self.packed_weight, scale, self.weight_scale, out_fp32=True)
+            dist.all_reduce(partial, group=self.group)
+            out = partial.to(torch.bfloat16)
+        return out.reshape(*x.shape[:-1], self.out_features)

@@ -1,0 +1,31 @@
+"""Shared helpers of the GPU parity tests: canary-guarded output buffers and
+conversions between torch tensors and the oracle's numpy arrays."""
+import numpy as np
+import torch
+
+
+def u16(t: torch.Tensor) -> np.ndarray:
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def u8(t: torch.Tensor) -> np.ndarray:
+    return t.detach().cpu().contiguous().view(torch.uint8).numpy()
+
+
+class Guarded:
+    """An output tensor carved out of a larger buffer whose 64-element margins
+    hold a canary value; ``intact()`` checks nothing was written outside."""
+
+    def __init__(self, shape, dtype, device, canary, fill):
+        n = int(np.prod(shape))
+        self.store = torch.full((n + 128,), canary, dtype=dtype, device=device)
+        self.head = self.store[:64].clone()
+        self.view = self.store[64:64 + n].view(*shape)
+        self.view.fill_(fill)
+
+    def intact(self) -> bool:
+        return bool(torch.equal(self.store[:64], self.head) and torch.equal(self.store[-64:], self.head))
+
+
+def bf16_bits_to_float(bits: np.ndarray) -> np.ndarray:
+    return (bits.astype(np.uint32) << 16).view(np.float32)
