@@ -46,15 +46,17 @@ METRIC = "W4A4 decode linears HBM GB/s (Qwen3-8B shapes, batch 32, 36 layers)"
 
 
 def linear_bytes(m: int, n: int, k: int) -> int:
-    """Algorithmic HBM bytes of one prep + GEMM chain: X read, codes and scales
-    written then read, weights and weight scales read, BF16 output written, signs."""
-    prep = 2 * m * k + k + (m * k // 2 + 2 * m * k // 128)
-    gemm = n * k // 2 + 2 * n * k // 128 + (m * k // 2 + 2 * m * k // 128) + 2 * m * n
-    return prep + gemm
+    """Algorithmic HBM bytes of one prep + GEMM chain: X read, codes (INT8 layout)
+    and scales written then read, weights and weight scales read, BF16 output
+    written, signs."""
+    prep = 2 * m * k + k + (m * k + 2 * m * k // 128)
+    return prep + gemm_bytes(m, n, k)
 
 
 def gemm_bytes(m: int, n: int, k: int) -> int:
-    return n * k // 2 + 2 * n * k // 128 + m * k // 2 + 2 * m * k // 128 + 2 * m * n
+    """Algorithmic bytes of one GEMM launch: packed weights + weight scales, INT8
+    activation codes + scales, BF16 output."""
+    return n * k // 2 + 2 * n * k // 128 + m * k + 2 * m * k // 128 + 2 * m * n
 
 
 def step_bytes(m: int, layers: int) -> int:
@@ -79,7 +81,7 @@ class ClockSampler(threading.Thread):
     def __init__(self, device_index: int, period_s: float = 0.005):
         super().__init__(daemon=True)
         self.samples, self.reasons, self.period = [], set(), period_s
-        self._stop = threading.Event()
+        self._halt = threading.Event()
         self.ok = False
         try:
             import pynvml
@@ -98,7 +100,7 @@ class ClockSampler(threading.Thread):
     def run(self):
         if not self.ok:
             return
-        while not self._stop.is_set():
+        while not self._halt.is_set():
             try:
                 self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
                 mask = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
@@ -110,7 +112,7 @@ class ClockSampler(threading.Thread):
             time.sleep(self.period)
 
     def stop(self):
-        self._stop.set()
+        self._halt.set()
         self.join(timeout=2)
         if not self.ok:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": getattr(self, "error", "nvml")}
@@ -307,7 +309,7 @@ def main():
 
     # roofline of the dominant kernel: the gate/up GEMM (N=24576, K=4096, M=32) on
     # this rank's shard, timed over one launch per layer (distinct weights)
-    from nanovllm.kernels.w4a4_grouped_kernel import w4a4_grouped_gemm
+    from nanovllm.kernels.w4a4_grouped_kernel import w4a4_grouped_gemm_i8 as w4a4_grouped_gemm
     gu = [layer["gate_up"] for layer in mods]
     with torch.no_grad():
         pa, sa = gu[0].quantize_input(x_dev)

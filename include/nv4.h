@@ -58,6 +58,18 @@ int nv4_rht_quant_pack(const void* x, const void* signs, void* out_packed, void*
                        int64_t k, int layout, int clamp_lo, void* stream);
 
 /*
+ * Same transform and quantisation as nv4_rht_quant_pack, but the codes are
+ * written as GEMM-ready INT8 for nv4_w4a4_gemm_i8 instead of packed nibbles:
+ *   out_codes int8 [m, k], 16-byte aligned; within every 32-wide K chunk the
+ *             16 codes of even k come first (in k order), then the 16 of odd k.
+ * The reference fuses nothing here; this is the first half of
+ * nanovllm/layers/linear_w4a4.py:27-36 (W4A4Linear.forward) with the
+ * intermediate in the layout the decode GEMM consumes without unpacking.
+ */
+int nv4_rht_quant_i8(const void* x, const void* signs, void* out_codes, void* out_scale, int64_t m, int64_t k,
+                     int layout, int clamp_lo, void* stream);
+
+/*
  * Grouped INT4 GEMM: out[m, n] = sum_g fp32-FMA(dot_g(a, w), sa[m,g] * sw[n,g]),
  * groups of 128 along K in increasing g, one FP32 rounding per group, then BF16.
  * Replaces nanovllm/kernels/w4a4_grouped_kernel.py:104-129 (w4a4_grouped_gemm)
@@ -72,6 +84,14 @@ int nv4_rht_quant_pack(const void* x, const void* signs, void* out_packed, void*
  */
 int nv4_w4a4_grouped_gemm(const void* a_packed, const void* w_packed, const void* a_scale, const void* w_scale,
                           void* out, int64_t m, int64_t n, int64_t k, int flags, void* stream);
+
+/*
+ * The grouped GEMM with activations from nv4_rht_quant_i8 (int8 [m, k] in that
+ * layout, 16-byte aligned) instead of packed nibbles; identical results.  The
+ * second half of nanovllm/layers/linear_w4a4.py:27-36 (W4A4Linear.forward).
+ */
+int nv4_w4a4_gemm_i8(const void* a_codes, const void* w_packed, const void* a_scale, const void* w_scale, void* out,
+                     int64_t m, int64_t n, int64_t k, int flags, void* stream);
 
 /*
  * Diagnostic: exact per-group INT32 dot products dots[g, m, n] of the same

@@ -80,26 +80,46 @@ int ensure_smem_attr(const void* kernel, int bytes, int* done_flags) {
   return NV4_OK;
 }
 
-bool make_tensor_map_u8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols_bytes, uint32_t box_rows,
-                        uint32_t box_cols_bytes, CUtensorMapSwizzle swizzle) {
+bool make_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base, uint64_t rows,
+                        uint64_t cols, uint32_t box_rows, uint32_t box_cols, CUtensorMapSwizzle swizzle) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return false;
-  const cuuint64_t dims[2] = {cols_bytes, rows};
-  const cuuint64_t strides[1] = {cols_bytes};
-  const cuuint32_t box[2] = {box_cols_bytes, box_rows};
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * static_cast<uint64_t>(elem_bytes)};
+  const cuuint32_t box[2] = {box_cols, box_rows};
   const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+  const CUresult r = enc(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
                          CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
-int launch_w4a4_stream_gemm(const void* a_packed, const void* w_packed, const void* a_scale, const void* w_scale,
-                            void* out, int64_t m, int64_t n, int64_t k, int flags, cudaStream_t stream);
+bool make_tensor_map_u8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols_bytes, uint32_t box_rows,
+                        uint32_t box_cols_bytes, CUtensorMapSwizzle swizzle) {
+  return make_tensor_map_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, base, rows, cols_bytes, box_rows, box_cols_bytes,
+                            swizzle);
+}
 
-int launch_w4a4_gemm(const void* a_packed, const void* w_packed, const void* a_scale, const void* w_scale, void* out,
-                     int64_t m, int64_t n, int64_t k, int flags, cudaStream_t stream) {
-  return launch_w4a4_stream_gemm(a_packed, w_packed, a_scale, w_scale, out, m, n, k, flags, stream);
+int launch_w4a4_stream_gemm(const void* a_packed, const void* a8, const void* w_packed, const void* a_scale,
+                            const void* w_scale, void* out, int64_t m, int64_t n, int64_t k, int flags,
+                            cudaStream_t stream);
+
+int launch_w4a4_tc_gemm(const void* a8, const void* w_packed, const void* a_scale, const void* w_scale, void* out,
+                        int64_t m, int64_t n, int64_t k, int flags, cudaStream_t stream);
+
+// Token counts above kTcMinTokens with INT8-layout activations go to the
+// tcgen05 kernel (tensor-bound prefill shapes); decode shapes, packed
+// activations and NV4_GEMM_FORCE_STREAM to the mma.sync weight-streaming
+// kernel, which keeps every SM streaming weights when there are few tokens.
+constexpr int64_t kTcMinTokens = 64;
+
+int launch_w4a4_gemm(const void* a_packed, const void* a8, const void* w_packed, const void* a_scale,
+                     const void* w_scale, void* out, int64_t m, int64_t n, int64_t k, int flags, cudaStream_t stream) {
+  if (a8 != nullptr && !(flags & NV4_GEMM_FORCE_STREAM) && m > kTcMinTokens) {
+    const int rc = launch_w4a4_tc_gemm(a8, w_packed, a_scale, w_scale, out, m, n, k, flags, stream);
+    if (rc != NV4_ERR_UNSUPPORTED) return rc;
+  }
+  return launch_w4a4_stream_gemm(a_packed, a8, w_packed, a_scale, w_scale, out, m, n, k, flags, stream);
 }
 
 }  // namespace nv4
@@ -142,10 +162,9 @@ int nv4_device_error(int* code) {
   return NV4_OK;
 }
 
-int nv4_rht_quant_pack(const void* x, const void* signs, void* out_packed, void* out_scale, int64_t m, int64_t k,
-                       int layout, int clamp_lo, void* stream) {
-  if (!x || !signs || !out_packed || !out_scale || m < 1 || m > (int64_t(1) << 31) - 1)
-    return NV4_ERR_INVALID_ARGUMENT;
+static int check_prep_args(const void* x, const void* signs, const void* codes, const void* scale, int64_t m,
+                           int64_t k, int layout, int clamp_lo, uintptr_t codes_align) {
+  if (!x || !signs || !codes || !scale || m < 1 || m > (int64_t(1) << 31) - 1) return NV4_ERR_INVALID_ARGUMENT;
   if (clamp_lo != -7 && clamp_lo != -8) return NV4_ERR_INVALID_ARGUMENT;
   if (layout == NV4_LAYOUT_BLOCK128) {
     if (k < 128 || k % 128 || k > (int64_t(1) << 24)) return NV4_ERR_INVALID_ARGUMENT;
@@ -154,25 +173,55 @@ int nv4_rht_quant_pack(const void* x, const void* signs, void* out_packed, void*
   } else {
     return NV4_ERR_INVALID_ARGUMENT;
   }
-  if (!aligned(x, 16) || !aligned(signs, 8) || !aligned(out_packed, 4) || !aligned(out_scale, 2))
+  if (!aligned(x, 16) || !aligned(signs, 8) || !aligned(codes, codes_align) || !aligned(scale, 2))
     return NV4_ERR_ALIGNMENT;
   if (!device_is_sm100()) return NV4_ERR_DEVICE;
-  return launch_rht_quant_pack(x, signs, out_packed, out_scale, m, k, layout, clamp_lo,
-                               static_cast<cudaStream_t>(stream));
+  return NV4_OK;
 }
 
-int nv4_w4a4_grouped_gemm(const void* a_packed, const void* w_packed, const void* a_scale, const void* w_scale,
-                          void* out, int64_t m, int64_t n, int64_t k, int flags, void* stream) {
-  if (!a_packed || !w_packed || !a_scale || !w_scale || !out) return NV4_ERR_INVALID_ARGUMENT;
+int nv4_rht_quant_pack(const void* x, const void* signs, void* out_packed, void* out_scale, int64_t m, int64_t k,
+                       int layout, int clamp_lo, void* stream) {
+  const int rc = check_prep_args(x, signs, out_packed, out_scale, m, k, layout, clamp_lo, 4);
+  if (rc != NV4_OK) return rc;
+  return launch_rht_quant(x, signs, out_packed, nullptr, out_scale, m, k, layout, clamp_lo,
+                          static_cast<cudaStream_t>(stream));
+}
+
+int nv4_rht_quant_i8(const void* x, const void* signs, void* out_codes, void* out_scale, int64_t m, int64_t k,
+                     int layout, int clamp_lo, void* stream) {
+  const int rc = check_prep_args(x, signs, out_codes, out_scale, m, k, layout, clamp_lo, 16);
+  if (rc != NV4_OK) return rc;
+  return launch_rht_quant(x, signs, nullptr, out_codes, out_scale, m, k, layout, clamp_lo,
+                          static_cast<cudaStream_t>(stream));
+}
+
+static int check_gemm_args(const void* a, const void* w_packed, const void* a_scale, const void* w_scale,
+                           const void* out, int64_t m, int64_t n, int64_t k, int flags) {
+  if (!a || !w_packed || !a_scale || !w_scale || !out) return NV4_ERR_INVALID_ARGUMENT;
   if (m < 1 || n < 1 || k < 128 || k % 128 || n % 8 || m > (int64_t(1) << 31) - 1 || n > (int64_t(1) << 31) - 1 ||
       k > (int64_t(1) << 24))
     return NV4_ERR_INVALID_ARGUMENT;
   if (flags & ~(NV4_GEMM_W_SCALE_GROUPED | NV4_GEMM_OUT_FP32 | NV4_GEMM_FORCE_STREAM)) return NV4_ERR_INVALID_ARGUMENT;
-  if (!aligned(a_packed, 16) || !aligned(w_packed, 16) || !aligned(a_scale, 2) || !aligned(w_scale, 2) ||
+  if (!aligned(a, 16) || !aligned(w_packed, 16) || !aligned(a_scale, 2) || !aligned(w_scale, 2) ||
       !aligned(out, (flags & NV4_GEMM_OUT_FP32) ? 4 : 2))
     return NV4_ERR_ALIGNMENT;
   if (!device_is_sm100()) return NV4_ERR_DEVICE;
-  return launch_w4a4_gemm(a_packed, w_packed, a_scale, w_scale, out, m, n, k, flags,
+  return NV4_OK;
+}
+
+int nv4_w4a4_grouped_gemm(const void* a_packed, const void* w_packed, const void* a_scale, const void* w_scale,
+                          void* out, int64_t m, int64_t n, int64_t k, int flags, void* stream) {
+  const int rc = check_gemm_args(a_packed, w_packed, a_scale, w_scale, out, m, n, k, flags);
+  if (rc != NV4_OK) return rc;
+  return launch_w4a4_gemm(a_packed, nullptr, w_packed, a_scale, w_scale, out, m, n, k, flags,
+                          static_cast<cudaStream_t>(stream));
+}
+
+int nv4_w4a4_gemm_i8(const void* a_codes, const void* w_packed, const void* a_scale, const void* w_scale, void* out,
+                     int64_t m, int64_t n, int64_t k, int flags, void* stream) {
+  const int rc = check_gemm_args(a_codes, w_packed, a_scale, w_scale, out, m, n, k, flags);
+  if (rc != NV4_OK) return rc;
+  return launch_w4a4_gemm(nullptr, a_codes, w_packed, a_scale, w_scale, out, m, n, k, flags,
                           static_cast<cudaStream_t>(stream));
 }
 

@@ -174,19 +174,96 @@ __device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t& r0, uint32_
                : "r"(addr));
 }
 
-// D = A(16x64 s4, row) * B(64x8 s4, col) + C, INT32 accumulate.
-__device__ __forceinline__ void mma_s4_16864(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+// D = A(16x32 s8, row) * B(32x8 s8, col) + C, INT32 accumulate (native on sm_100;
+// the s4 form of mma.sync is not, so INT4 operands are widened to INT8 first).
+__device__ __forceinline__ void mma_s8_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
   asm volatile(
-      "mma.sync.aligned.m16n8k64.row.col.s32.s4.s4.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
       "{%0, %1, %2, %3};"
       : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
+
+// INT4 -> INT8 widening of a packed word (8 codes, code i in nibble i).  Each
+// code c becomes the int8 16*c, exact for c in [-8, 7]:
+//   nib_even16: bytes (16*c0, 16*c2, 16*c4, 16*c6)
+//   nib_odd16:  bytes (16*c1, 16*c3, 16*c5, 16*c7)
+__device__ __forceinline__ uint32_t nib_even16(uint32_t p) { return (p << 4) & 0xF0F0F0F0u; }
+__device__ __forceinline__ uint32_t nib_odd16(uint32_t p) { return p & 0xF0F0F0F0u; }
 
 // Byte offset of 16-byte chunk `chunk` (0..7) of row `row` in a 128-byte-row
 // tile written by TMA with CU_TENSOR_MAP_SWIZZLE_128B (1024-byte aligned tile).
 __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t chunk) {
   return row * 128u + ((chunk ^ (row & 7u)) << 4);
 }
+
+// ----------------------------------------------------------------- tcgen05 (5th-gen tensor cores)
+// Shared-memory matrix descriptor for a K-major operand stored as 128-byte rows
+// with the 128-byte swizzle (8-row, 1024-byte atoms): start address >> 4 in
+// bits 0-13, leading-dimension offset 16 B (unused for this layout) in bits
+// 16-29, stride between 8-row atoms (1024 B) in bits 32-45, descriptor version
+// 1 in bits 46-47, layout SWIZZLE_128B (2) in bits 61-63.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr) {
+  return (static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu)) | (static_cast<uint64_t>(1u) << 16) |
+         (static_cast<uint64_t>(1024u >> 4) << 32) | (static_cast<uint64_t>(1u) << 46) |
+         (static_cast<uint64_t>(2u) << 61);
+}
+
+// Instruction descriptor of tcgen05.mma kind::i8: signed 8-bit A and B, both
+// K-major, S32 accumulator, M x N.
+__host__ __device__ constexpr uint32_t umma_idesc_s8(int m, int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* smem_dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_dst)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, one instruction issued by one thread.
+__device__ __forceinline__ void umma_s8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.u32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on `bar` once every tcgen05 operation issued so far by this thread completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 32 lanes x 16 columns of 32-bit TMEM -> 16 registers per thread (lane = thread).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15},"
+      " [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, uint32_t v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};"
+      ::"r"(taddr), "r"(v)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 }  // namespace nv4

@@ -50,12 +50,16 @@ int ensure_smem_attr(const void* kernel, int bytes, int* done_flags /* [64] */);
 // [box_rows, box_cols_bytes] and the given swizzle; false on failure.
 bool make_tensor_map_u8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols_bytes, uint32_t box_rows,
                         uint32_t box_cols_bytes, CUtensorMapSwizzle swizzle);
+bool make_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base, uint64_t rows,
+                        uint64_t cols, uint32_t box_rows, uint32_t box_cols, CUtensorMapSwizzle swizzle);
 
 // ---- launchers (one per kernel family) ----
-int launch_rht_quant_pack(const void* x, const void* signs, void* packed, void* scale, int64_t m, int64_t k,
-                          int layout, int clamp_lo, cudaStream_t stream);
-int launch_w4a4_gemm(const void* a_packed, const void* w_packed, const void* a_scale, const void* w_scale, void* out,
-                     int64_t m, int64_t n, int64_t k, int flags, cudaStream_t stream);
+// Activation prep; `packed` and/or `codes8` (GEMM-ready INT8 layout) receive the codes.
+int launch_rht_quant(const void* x, const void* signs, void* packed, void* codes8, void* scale, int64_t m, int64_t k,
+                     int layout, int clamp_lo, cudaStream_t stream);
+// Grouped GEMM; activations from `a8` (INT8 layout) when non-null, else `a_packed`.
+int launch_w4a4_gemm(const void* a_packed, const void* a8, const void* w_packed, const void* a_scale,
+                     const void* w_scale, void* out, int64_t m, int64_t n, int64_t k, int flags, cudaStream_t stream);
 int launch_w4a4_group_dots(const void* a_packed, const void* w_packed, int32_t* dots, int64_t m, int64_t n, int64_t k,
                            cudaStream_t stream);
 int launch_w4a16_gemm(const void* x, const void* qweight, const void* qzeros, const void* scales, void* out,

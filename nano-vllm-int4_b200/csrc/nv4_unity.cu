@@ -2,4 +2,5 @@
 #include "nv4_capi.cu"
 #include "rht_quant.cu"
 #include "w4a4_gemm.cu"
+#include "w4a4_gemm_tc.cu"
 #include "w4a16_gemm.cu"

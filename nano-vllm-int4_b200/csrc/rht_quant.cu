@@ -49,11 +49,41 @@ __device__ __forceinline__ float round_scale(float s, uint16_t* bits) {
   return __bfloat162float(b);
 }
 
-__device__ __forceinline__ uint32_t code_nibble(float v, float sf, int clamp_lo) {
+__device__ __forceinline__ int quant_code(float v, float sf, int clamp_lo) {
   int c = __float2int_rn(__fdiv_rn(v, sf));
   c = max(c, clamp_lo);
-  c = min(c, 7);
-  return static_cast<uint32_t>(c) & 15u;
+  return min(c, 7);
+}
+
+// Quantise the 8 values of k = k8 .. k8+7 (k8 % 8 == 0) of one row and store
+// them in the requested forms:
+//  * packed (two codes per byte, even k in the low nibble) at packed_row + k8/2;
+//  * GEMM-ready INT8 codes (i8_row != nullptr): within each 32-wide K chunk the
+//    16 even-k codes come first, then the 16 odd-k codes -- the K order the
+//    GEMM's INT4->INT8 weight widening produces, so its MMA operands match.
+__device__ __forceinline__ void store_codes(const float (&v)[8], float sf, int clamp_lo, uint8_t* packed_row,
+                                            int8_t* i8_row, int k8) {
+  int c[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) c[e] = quant_code(v[e], sf, clamp_lo);
+  if (packed_row != nullptr) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) word |= (static_cast<uint32_t>(c[e]) & 15u) << (4 * e);
+    *reinterpret_cast<uint32_t*>(packed_row + k8 / 2) = word;
+  }
+  if (i8_row != nullptr) {
+    uint32_t even = 0, odd = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      even |= (static_cast<uint32_t>(c[2 * i]) & 255u) << (8 * i);
+      odd |= (static_cast<uint32_t>(c[2 * i + 1]) & 255u) << (8 * i);
+    }
+    int8_t* chunk = i8_row + (k8 & ~31);
+    const int q = (k8 & 31) >> 3;
+    *reinterpret_cast<uint32_t*>(chunk + q * 4) = even;
+    *reinterpret_cast<uint32_t*>(chunk + 16 + q * 4) = odd;
+  }
 }
 
 // Load 8 BF16 values (16 bytes) and apply 8 sign bits (bit e set = negate).
@@ -104,7 +134,8 @@ __device__ __forceinline__ float butterfly_lane(float v, int mask, bool high) {
 struct Block128Args {
   const uint16_t* x;
   const int8_t* signs;
-  uint8_t* packed;
+  uint8_t* packed;   // or nullptr
+  int8_t* codes8;    // or nullptr
   uint16_t* scale;
   int M, K, G, ncb, warps_used, clamp_lo;
 };
@@ -181,14 +212,10 @@ __global__ void __launch_bounds__(256) rht_block128_kernel(const Block128Args p)
     uint16_t sbits;
     const float sf = round_scale(scale_block128(mx), &sbits);
     if (active) {
-      uint8_t* dst = p.packed + static_cast<size_t>(row) * (p.K / 2) + g * 64 + q * 4;
+      uint8_t* prow = p.packed ? p.packed + static_cast<size_t>(row) * (p.K / 2) : nullptr;
+      int8_t* irow = p.codes8 ? p.codes8 + static_cast<size_t>(row) * p.K : nullptr;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint32_t word = 0;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) word |= code_nibble(v[j][e], sf, p.clamp_lo) << (4 * e);
-        *reinterpret_cast<uint32_t*>(dst + j * 16) = word;
-      }
+      for (int j = 0; j < 4; ++j) store_codes(v[j], sf, p.clamp_lo, prow, irow, g * 128 + j * 32 + q * 8);
       if (q == 0) p.scale[static_cast<size_t>(row) * p.G + g] = sbits;
     }
   }
@@ -198,7 +225,8 @@ __global__ void __launch_bounds__(256) rht_block128_kernel(const Block128Args p)
 struct RowDHArgs {
   const uint16_t* x;
   const int8_t* signs;
-  uint8_t* packed;
+  uint8_t* packed;   // or nullptr
+  int8_t* codes8;    // or nullptr
   uint16_t* scale;
   int M, clamp_lo;
 };
@@ -275,7 +303,8 @@ __global__ void __launch_bounds__(128) rht_rowdh4096_kernel(const RowDHArgs p) {
     }
     __syncthreads();
     // groups: k >> 7 = w*8 + j*2 + (l >> 4); 16 lanes x 8 values each
-    uint8_t* dst = p.packed + static_cast<size_t>(row) * (K / 2) + (w * 1024 + l * 8) / 2;
+    uint8_t* prow = p.packed ? p.packed + static_cast<size_t>(row) * (K / 2) : nullptr;
+    int8_t* irow = p.codes8 ? p.codes8 + static_cast<size_t>(row) * K : nullptr;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       float mx = 0.0f;
@@ -285,10 +314,7 @@ __global__ void __launch_bounds__(128) rht_rowdh4096_kernel(const RowDHArgs p) {
       for (int m = 1; m < 16; m <<= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, m));
       uint16_t sbits;
       const float sf = round_scale(scale_rowdh(mx), &sbits);
-      uint32_t word = 0;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) word |= code_nibble(v[j][e], sf, p.clamp_lo) << (4 * e);
-      *reinterpret_cast<uint32_t*>(dst + j * 128) = word;
+      store_codes(v[j], sf, p.clamp_lo, prow, irow, w * 1024 + j * 256 + l * 8);
       if ((l & 15) == 0) p.scale[static_cast<size_t>(row) * G + w * 8 + j * 2 + (l >> 4)] = sbits;
     }
   }
@@ -362,7 +388,8 @@ __global__ void __launch_bounds__(128) rht_rowdh12288_kernel(const RowDHArgs p) 
 #pragma unroll
       for (int d = 0; d < 12; ++d) v[d][e] = b[d];
     }
-    uint8_t* dst = p.packed + static_cast<size_t>(row) * (K / 2) + (w * 256 + l * 8) / 2;
+    uint8_t* prow = p.packed ? p.packed + static_cast<size_t>(row) * (K / 2) : nullptr;
+    int8_t* irow = p.codes8 ? p.codes8 + static_cast<size_t>(row) * K : nullptr;
 #pragma unroll
     for (int f = 0; f < 12; ++f) {
       float mx = 0.0f;
@@ -372,10 +399,7 @@ __global__ void __launch_bounds__(128) rht_rowdh12288_kernel(const RowDHArgs p) 
       for (int m = 1; m < 16; m <<= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, m));
       uint16_t sbits;
       const float sf = round_scale(scale_rowdh(mx), &sbits);
-      uint32_t word = 0;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) word |= code_nibble(v[f][e], sf, p.clamp_lo) << (4 * e);
-      *reinterpret_cast<uint32_t*>(dst + f * 512) = word;
+      store_codes(v[f], sf, p.clamp_lo, prow, irow, f * 1024 + w * 256 + l * 8);
       if ((l & 15) == 0) p.scale[static_cast<size_t>(row) * G + f * 8 + w * 2 + (l >> 4)] = sbits;
     }
   }
@@ -384,8 +408,9 @@ __global__ void __launch_bounds__(128) rht_rowdh12288_kernel(const RowDHArgs p) 
 // ============================================================ host launchers
 constexpr int kRowDH12288Smem = padded(12288) * 4;
 
-int launch_rht_quant_pack(const void* x, const void* signs, void* packed, void* scale, int64_t m, int64_t k,
-                          int layout, int clamp_lo, cudaStream_t stream) {
+// `packed` and/or `codes8` receive the codes (at least one is non-null).
+int launch_rht_quant(const void* x, const void* signs, void* packed, void* codes8, void* scale, int64_t m, int64_t k,
+                     int layout, int clamp_lo, cudaStream_t stream) {
   const int sms = device_sm_count();
   if (sms <= 0) return NV4_ERR_CUDA;
   if (layout == NV4_LAYOUT_BLOCK128) {
@@ -393,6 +418,7 @@ int launch_rht_quant_pack(const void* x, const void* signs, void* packed, void* 
     a.x = static_cast<const uint16_t*>(x);
     a.signs = static_cast<const int8_t*>(signs);
     a.packed = static_cast<uint8_t*>(packed);
+    a.codes8 = static_cast<int8_t*>(codes8);
     a.scale = static_cast<uint16_t*>(scale);
     a.M = static_cast<int>(m);
     a.K = static_cast<int>(k);
@@ -410,6 +436,7 @@ int launch_rht_quant_pack(const void* x, const void* signs, void* packed, void* 
   a.x = static_cast<const uint16_t*>(x);
   a.signs = static_cast<const int8_t*>(signs);
   a.packed = static_cast<uint8_t*>(packed);
+  a.codes8 = static_cast<int8_t*>(codes8);
   a.scale = static_cast<uint16_t*>(scale);
   a.M = static_cast<int>(m);
   a.clamp_lo = clamp_lo;

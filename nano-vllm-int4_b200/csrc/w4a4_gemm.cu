@@ -7,19 +7,32 @@
 // result is multiplied by sw[n] at the end.  There is no split-K: each output
 // element's FMA chain runs in one thread, in group order.
 //
-// Design: the weights are the streamed operand.  Each CTA owns R weight rows
-// (a multiple of 16, chosen so the grid is about one CTA per SM) and all K.
-// A producer warp streams [R x 256-K] packed weight tiles and the matching
-// [MT*8 x 256-K] packed activation tiles into a ring of shared-memory stages
-// with 2-D TMA copies (128-byte swizzle, no multicast), completion tracked by
-// mbarriers.  Four consumer warps read fragments with ldmatrix straight from
-// the packed nibbles (the packed layout is exactly the s4 MMA operand layout)
-// and issue mma.sync m16n8k64 s4 with weights as the 16-row operand and tokens
-// as the 8-column operand.  The INT32 accumulator starts at the bit pattern of
-// 1.5*2^23, so after a group it reads as the float 12582912 + dot exactly and
-// the conversion costs one FADD.  The weight tiles for the first stages are
-// requested before griddepcontrol.wait, so with programmatic dependent launch
-// the weight stream overlaps the activation-prep kernel that precedes it.
+// Design: the weights are the streamed operand.  A CTA owns R = 16*S weight
+// rows (S "slabs", chosen so the grid is about one CTA per SM) and all of K.
+// One producer warp streams [R x 256-K] packed weight tiles, and the matching
+// activation tiles, into a ring of shared-memory stages with 2-D TMA copies
+// (128-byte swizzle, no multicast); mbarriers track completion.  The weight
+// tiles of the first stages and the weight scales are requested before
+// griddepcontrol.wait, so under programmatic dependent launch they stream
+// while the activation-prep kernel before this one is still running.
+//
+// Each consumer warp owns one 16-row slab (and, for narrow layers, a share of
+// the token tiles).  It reads packed weight fragments with ldmatrix, widens
+// the nibbles to INT8 in registers (16*code, even K then odd K of each 8-code
+// word) and issues mma.sync m16n8k32 s8 (INT4 mma.sync is not native on
+// sm_100).  Activations arrive either already widened (the "A8" layout the
+// prep kernel writes: INT8 codes with the same even/odd K order, so ldmatrix
+// yields MMA fragments directly) or packed (widened in registers).
+//
+// Epilogue per group: the INT32 accumulator starts at the bit pattern of
+// 1.5*2^23 and reads as the float 12582912 + 16*dot.  When both scales are in
+// a range where sa*sw is exact in FP32 (always, for the quantizer's scales),
+//   ds = fma(F, sa/16, -786432*sa) = dot*sa  (exact)   and
+//   total = fma(ds, sw, total)                 (= fma(dot, sa*sw, total)),
+// two FMAs per element, with the per-token pair (sa/16, -786432*sa) computed
+// once per CTA.  Otherwise the reference's three-step form is used.
+#include <cstring>
+
 #include "nv4_device.cuh"
 #include "nv4_launch.h"
 
@@ -30,19 +43,14 @@ struct StreamGemmArgs {
   const uint16_t* w_scale;  // bf16 [N, G] (grouped) or [N]
   void* out;                // bf16 or fp32 [M, N]
   int M, N, G;
-  int R;        // weight rows per CTA (multiple of 16, <= 256)
-  int n_iters;  // pipeline iterations = ceil(G / 2) (two groups per stage)
+  int R;          // weight rows per CTA (16 * slabs)
+  int slabs;      // R / 16
+  int n_iters;    // ceil(G / 2): two groups per stage
   int stages;
+  int scale_tma;  // 1: weight/activation scales arrive by TMA (G % 8 == 0)
 };
 
-constexpr int kConsumerWarps = 4;
-constexpr int kStreamThreads = 32 * (1 + kConsumerWarps);
-constexpr int kMaxSlabsPerWarp = 4;  // R <= 256 -> 16 slabs of 16 rows
-
-struct StreamSmem {
-  uint32_t base;  // 1024-aligned shared address of stage 0
-  int stage_bytes, w_bytes;
-};
+constexpr int kMaxConsumerWarps = 16;
 
 __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
   const uint64_t start = global_timer_ns();
@@ -55,32 +63,64 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) 
   return true;
 }
 
-template <int MT, bool WGROUPED, bool OUT_F32>
-__global__ void __launch_bounds__(kStreamThreads, 1)
+__device__ __forceinline__ bool scale_in_fast_range(float s, float lo, float hi) {
+  const float a = fabsf(s);
+  return a == 0.0f || (a >= lo && a <= hi);
+}
+
+// Shared-memory carve-up (byte offsets from the 1024-aligned base).
+struct StreamLayout {
+  int w_bytes, a_bytes, stage_bytes, sw_off, sa_off, sac_off, flags_off, bar_off, total;
+  __host__ __device__ StreamLayout(int R, int MP, int G, int S, bool wg) {
+    w_bytes = R * 128;
+    a_bytes = MP * 128;  // per group (A8) or per stage (packed)
+    stage_bytes = w_bytes + 2 * a_bytes;
+    sw_off = S * stage_bytes;
+    const int sw_bytes = (wg ? R * G : R) * 2;
+    sa_off = (sw_off + sw_bytes + 1023) & ~1023;
+    sac_off = (sa_off + MP * G * 2 + 15) & ~15;
+    flags_off = sac_off + MP * G * 8;
+    bar_off = (flags_off + 2 * G * 4 + 7) & ~7;
+    total = bar_off + (2 * S + 2) * 8 + 16;
+  }
+};
+
+// MT: token tiles of 8 per CTA; TPW: token tiles per consumer warp;
+// A8: activations in the widened layout; WG: grouped weight scales; F32: FP32 out.
+template <int MT, int TPW, bool A8, bool WG, bool F32>
+__global__ void __launch_bounds__(32 * (1 + kMaxConsumerWarps), 1)
     w4a4_stream_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
+                       const __grid_constant__ CUtensorMap tmap_sw, const __grid_constant__ CUtensorMap tmap_sa,
                        const StreamGemmArgs p) {
-  constexpr int MP = MT * 8;  // token rows per tile
+  constexpr int MP = MT * 8;
+  constexpr int TS = MT / TPW;        // token splits per slab
+  constexpr int GI = TPW >= 4 ? 1 : 2;  // groups whose MMAs are interleaved
   extern __shared__ uint8_t smem_raw[];
   const int S = p.stages, R = p.R, G = p.G;
   const uint32_t raw = smem_u32(smem_raw);
-  const uint32_t pad = ((raw + 1023u) & ~1023u) - raw;
-  uint8_t* smem = smem_raw + pad;
-  const int w_bytes = R * 128, stage_bytes = w_bytes + MP * 128;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * stage_bytes);
+  uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  const StreamLayout L(R, MP, G, S, WG);
+  uint16_t* sw_s = reinterpret_cast<uint16_t*>(smem + L.sw_off);   // [R][G] (or [R])
+  uint16_t* sa_s = reinterpret_cast<uint16_t*>(smem + L.sa_off);   // [MP][G]
+  float2* sac = reinterpret_cast<float2*>(smem + L.sac_off);       // [G][MP]: (sa/16, -786432*sa)
+  int* fast_g = reinterpret_cast<int*>(smem + L.flags_off);        // [G]: both scales in range
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
   uint64_t* empty = full + S;
-  int* issued = reinterpret_cast<int*>(empty + S);
-  uint16_t* sw_s = reinterpret_cast<uint16_t*>(issued + 4);            // [G][R] (or [R])
-  float* sa_s = reinterpret_cast<float*>(sw_s + (WGROUPED ? G * R : R) + 8);  // [G][MP]
-  sa_s = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(sa_s) + 15) & ~uintptr_t(15));
+  uint64_t* scale_bar = empty + S;      // [0]: weight scales, [1]: activation scales
+  int* issued = reinterpret_cast<int*>(scale_bar + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int consumer_warps = p.slabs * TS;
   const int n0 = blockIdx.x * R, m0 = blockIdx.y * MP;
+  const uint32_t a_tile_bytes = A8 ? 2u * L.a_bytes : static_cast<uint32_t>(L.a_bytes);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumerWarps);
+      mbar_init(&empty[s], consumer_warps);
     }
+    mbar_init(&scale_bar[0], 1);
+    mbar_init(&scale_bar[1], 1);
     *issued = 0;
     fence_mbar_init();
   }
@@ -92,21 +132,50 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       tma_prefetch_desc(&tmap_w);
       tma_prefetch_desc(&tmap_a);
       const uint64_t wpol = policy_evict_first();
-      const uint32_t bytes = static_cast<uint32_t>(stage_bytes);
-      const int first = min(S, p.n_iters);
-      for (int s = 0; s < first; ++s) {
-        mbar_arrive_expect_tx(&full[s], bytes);
-        tma_load_2d_hint(smem + s * stage_bytes, &tmap_w, &full[s], s * 128, n0, wpol);
+      if (p.scale_tma) {
+        mbar_arrive_expect_tx(&scale_bar[0], static_cast<uint32_t>((WG ? R * G : R) * 2));
+        if (WG)
+          tma_load_2d(sw_s, &tmap_sw, &scale_bar[0], 0, n0);
+        else
+          tma_load_2d(sw_s, &tmap_sw, &scale_bar[0], n0, 0);
       }
-      grid_dependency_wait();  // activations come from the preceding kernel
-      for (int s = 0; s < first; ++s) tma_load_2d(smem + s * stage_bytes + w_bytes, &tmap_a, &full[s], s * 128, m0);
+      const uint32_t bytes = static_cast<uint32_t>(L.w_bytes) + a_tile_bytes;
+      const int first = min(S, p.n_iters);
+      // A CTA's TMA requests are served roughly in order, so only a couple of
+      // weight stages go out ahead of the activation scales: the consumers
+      // need those scales before their first group.
+      const int early = min(first, 2);
+      for (int s = 0; s < early; ++s) {
+        mbar_arrive_expect_tx(&full[s], bytes);
+        tma_load_2d_hint(smem + s * L.stage_bytes, &tmap_w, &full[s], s * 128, n0, wpol);
+      }
+      grid_dependency_wait();  // activations and their scales come from the preceding kernel
+      if (p.scale_tma) {
+        mbar_arrive_expect_tx(&scale_bar[1], static_cast<uint32_t>(MP * G * 2));
+        tma_load_2d(sa_s, &tmap_sa, &scale_bar[1], 0, m0);
+      }
+      auto load_a = [&](int slot, int it) {
+        uint8_t* dst = smem + slot * L.stage_bytes + L.w_bytes;
+        if (A8) {
+          tma_load_2d(dst, &tmap_a, &full[slot], it * 256, m0);
+          tma_load_2d(dst + L.a_bytes, &tmap_a, &full[slot], it * 256 + 128, m0);
+        } else {
+          tma_load_2d(dst, &tmap_a, &full[slot], it * 128, m0);
+        }
+      };
+      for (int s = 0; s < early; ++s) load_a(s, s);
+      for (int s = early; s < first; ++s) {
+        mbar_arrive_expect_tx(&full[s], bytes);
+        tma_load_2d_hint(smem + s * L.stage_bytes, &tmap_w, &full[s], s * 128, n0, wpol);
+        load_a(s, s);
+      }
       *reinterpret_cast<volatile int*>(issued) = first;
       for (int it = S; it < p.n_iters; ++it) {
         const int slot = it % S;
         if (!mbar_wait(&empty[slot], ((it / S) - 1) & 1, kErrTimeoutEmpty)) break;
         mbar_arrive_expect_tx(&full[slot], bytes);
-        tma_load_2d_hint(smem + slot * stage_bytes, &tmap_w, &full[slot], it * 128, n0, wpol);
-        tma_load_2d(smem + slot * stage_bytes + w_bytes, &tmap_a, &full[slot], it * 128, m0);
+        tma_load_2d_hint(smem + slot * L.stage_bytes, &tmap_w, &full[slot], it * 128, n0, wpol);
+        load_a(slot, it);
         *reinterpret_cast<volatile int*>(issued) = it + 1;
       }
     }
@@ -114,91 +183,178 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   }
 
   // ---------------- consumers
-  const int ct = threadIdx.x - 32;
   const int cw = warp - 1;
+  const int ct = threadIdx.x - 32, cthreads = 32 * consumer_warps;
+  const bool active = cw < consumer_warps;
+  const int slab = cw / TS, tile0 = (cw % TS) * TPW;
   const int gid = lane >> 2, tig = lane & 3;
-  if (WGROUPED) {
-    for (int i = ct; i < R * G; i += 32 * kConsumerWarps) {
-      const int r = i / G, g = i - r * G;
-      sw_s[g * R + r] = (n0 + r < p.N) ? p.w_scale[static_cast<size_t>(n0 + r) * G + g] : uint16_t(0);
+
+  // Scales: by TMA when the rows are 16-byte multiples, else cooperative loads.
+  // No early return before the named barriers: every consumer reaches them.
+  bool ok = true;
+  if (!p.scale_tma) {
+    if (active) {
+      const int nsw = WG ? R * G : R;
+      for (int i = ct; i < nsw; i += cthreads) {
+        const int r = WG ? i / G : i;
+        sw_s[i] = (n0 + r < p.N) ? p.w_scale[static_cast<size_t>(n0) * (WG ? G : 1) + i] : uint16_t(0);
+      }
     }
   } else {
-    for (int r = ct; r < R; r += 32 * kConsumerWarps) sw_s[r] = (n0 + r < p.N) ? p.w_scale[n0 + r] : uint16_t(0);
+    ok = mbar_wait(&scale_bar[0], 0, kErrTimeoutFull);
   }
+  for (int g = ct; g < G; g += cthreads) fast_g[g] = 1;
   grid_dependency_wait();
-  for (int i = ct; i < MP * G; i += 32 * kConsumerWarps) {
-    const int t = i / G, g = i - t * G;
-    sa_s[g * MP + t] = (m0 + t < p.M) ? bf16_bits_to_f32(p.a_scale[static_cast<size_t>(m0 + t) * G + g]) : 0.0f;
+  if (!p.scale_tma) {
+    if (active)
+      for (int i = ct; i < MP * G; i += cthreads)
+        sa_s[i] = (m0 + i / G < p.M) ? p.a_scale[static_cast<size_t>(m0) * G + i] : uint16_t(0);
+  } else {
+    ok = mbar_wait(&scale_bar[1], 0, kErrTimeoutFull) && ok;
   }
-  named_barrier_sync(1, 32 * kConsumerWarps);
+  named_barrier_sync(1, cthreads);
+  // Per-token epilogue constants; a group leaves the two-FMA path if any of its
+  // scales is out of range (every thread checks a slice; clearing is idempotent).
+  if (active) {
+    for (int i = ct; i < MP * G; i += cthreads) {
+      const int t = i / G, g = i - t * G;
+      const float sa = bf16_bits_to_f32(sa_s[i]);
+      sac[g * MP + t] = make_float2(__fmul_rn(sa, 0.0625f), __fmul_rn(sa, -786432.0f));
+      if (!scale_in_fast_range(sa, 0x1.0p-100f, 0x1.0p+100f)) fast_g[g] = 0;
+    }
+    if (WG)
+      for (int i = ct; i < R * G; i += cthreads)
+        if (!scale_in_fast_range(bf16_bits_to_f32(sw_s[i]), 0x1.0p-30f, 0x1.0p+27f)) fast_g[i % G] = 0;
+  }
+  named_barrier_sync(1, cthreads);
+  if (!active) return;
 
-  const int nslab = R / 16;
-  float tot[kMaxSlabsPerWarp][MT][4];
+  float tot[TPW][4];
 #pragma unroll
-  for (int s = 0; s < kMaxSlabsPerWarp; ++s)
+  for (int t = 0; t < TPW; ++t)
 #pragma unroll
-    for (int t = 0; t < MT; ++t)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) tot[s][t][i] = 0.0f;
+    for (int i = 0; i < 4; ++i) tot[t][i] = 0.0f;
 
   const uint32_t sbase = smem_u32(smem);
+  const int row_lo = slab * 16 + gid, row_hi = row_lo + 8;
   int it = 0;
-  bool ok = true;
-  for (; it < p.n_iters; ++it) {
+  for (; ok && it < p.n_iters; ++it) {
     const int slot = it % S;
     if (!mbar_wait(&full[slot], (it / S) & 1, kErrTimeoutFull)) {
       ok = false;
       break;
     }
-    const uint32_t wbase = sbase + slot * stage_bytes, abase = wbase + w_bytes;
+    const uint32_t wbase = sbase + slot * L.stage_bytes, abase = wbase + L.w_bytes;
+    // GI groups are processed together so that GI * TPW independent MMA chains
+    // are in flight; all fragment loads of a batch are issued before its MMAs.
 #pragma unroll
-    for (int gg = 0; gg < 2; ++gg) {
-      const int g = it * 2 + gg;
-      if (g >= G) break;
-      uint32_t bf[MT][4];
+    for (int gb = 0; gb < 2; gb += GI) {
+      uint32_t aw[GI][4][4];       // widened weight fragments [group][k32 step][a0..a3]
+      uint32_t bq[GI][TPW][8];     // token fragments [group][tile][k32 step x (b0, b1)]
+      const uint32_t lrow = slab * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
 #pragma unroll
-      for (int tt = 0; tt < MT; ++tt)
-        ldmatrix_x4(abase + sw128_offset(tt * 8 + (lane & 7), gg * 4 + (lane >> 3)), bf[tt][0], bf[tt][1],
-                    bf[tt][2], bf[tt][3]);
-      float sa0[MT], sa1[MT];
+      for (int gi = 0; gi < GI; ++gi) {
+        const int gg = gb + gi;
+        uint32_t af[2][4];
+        ldmatrix_x4(wbase + sw128_offset(lrow, gg * 4 + (lane >> 4)), af[0][0], af[0][1], af[0][2], af[0][3]);
+        ldmatrix_x4(wbase + sw128_offset(lrow, gg * 4 + 2 + (lane >> 4)), af[1][0], af[1][1], af[1][2], af[1][3]);
 #pragma unroll
-      for (int tt = 0; tt < MT; ++tt) {
-        const float2 v = *reinterpret_cast<const float2*>(sa_s + g * MP + tt * 8 + tig * 2);
-        sa0[tt] = v.x;
-        sa1[tt] = v.y;
-      }
+        for (int t = 0; t < TPW; ++t) {
+          const uint32_t trow = (tile0 + t) * 8 + (lane & 7);
+          if (A8) {
+            const uint32_t ab = abase + gg * L.a_bytes;
+            ldmatrix_x4(ab + sw128_offset(trow, lane >> 3), bq[gi][t][0], bq[gi][t][1], bq[gi][t][2], bq[gi][t][3]);
+            ldmatrix_x4(ab + sw128_offset(trow, 4 + (lane >> 3)), bq[gi][t][4], bq[gi][t][5], bq[gi][t][6],
+                        bq[gi][t][7]);
+          } else {
+            uint32_t bf[4];
+            ldmatrix_x4(abase + sw128_offset(trow, gg * 4 + (lane >> 3)), bf[0], bf[1], bf[2], bf[3]);
 #pragma unroll
-      for (int si = 0; si < kMaxSlabsPerWarp; ++si) {
-        const int slab = cw + kConsumerWarps * si;
-        if (slab >= nslab) break;
-        uint32_t af0[4], af1[4];
-        const uint32_t row = slab * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-        ldmatrix_x4(wbase + sw128_offset(row, gg * 4 + (lane >> 4)), af0[0], af0[1], af0[2], af0[3]);
-        ldmatrix_x4(wbase + sw128_offset(row, gg * 4 + 2 + (lane >> 4)), af1[0], af1[1], af1[2], af1[3]);
-        float sw0 = 0.0f, sw1 = 0.0f;
-        if (WGROUPED) {
-          sw0 = bf16_bits_to_f32(sw_s[g * R + slab * 16 + gid]);
-          sw1 = bf16_bits_to_f32(sw_s[g * R + slab * 16 + gid + 8]);
+            for (int w = 0; w < 4; ++w) {
+              bq[gi][t][2 * w] = nib_even16(bf[w]);
+              bq[gi][t][2 * w + 1] = nib_odd16(bf[w]);
+            }
+          }
         }
 #pragma unroll
-        for (int tt = 0; tt < MT; ++tt) {
-          int acc[4] = {kMagicBits, kMagicBits, kMagicBits, kMagicBits};
-          mma_s4_16864(acc, af0, bf[tt][0], bf[tt][1]);
-          mma_s4_16864(acc, af1, bf[tt][2], bf[tt][3]);
-          const float d0 = __fsub_rn(__int_as_float(acc[0]), kMagic);
-          const float d1 = __fsub_rn(__int_as_float(acc[1]), kMagic);
-          const float d2 = __fsub_rn(__int_as_float(acc[2]), kMagic);
-          const float d3 = __fsub_rn(__int_as_float(acc[3]), kMagic);
-          if (WGROUPED) {
-            tot[si][tt][0] = fmaf(d0, __fmul_rn(sa0[tt], sw0), tot[si][tt][0]);
-            tot[si][tt][1] = fmaf(d1, __fmul_rn(sa1[tt], sw0), tot[si][tt][1]);
-            tot[si][tt][2] = fmaf(d2, __fmul_rn(sa0[tt], sw1), tot[si][tt][2]);
-            tot[si][tt][3] = fmaf(d3, __fmul_rn(sa1[tt], sw1), tot[si][tt][3]);
+        for (int h = 0; h < 2; ++h) {
+          aw[gi][2 * h][0] = nib_even16(af[h][0]);
+          aw[gi][2 * h][1] = nib_even16(af[h][1]);
+          aw[gi][2 * h][2] = nib_odd16(af[h][0]);
+          aw[gi][2 * h][3] = nib_odd16(af[h][1]);
+          aw[gi][2 * h + 1][0] = nib_even16(af[h][2]);
+          aw[gi][2 * h + 1][1] = nib_even16(af[h][3]);
+          aw[gi][2 * h + 1][2] = nib_odd16(af[h][2]);
+          aw[gi][2 * h + 1][3] = nib_odd16(af[h][3]);
+        }
+      }
+      int acc[GI][TPW][4];
+#pragma unroll
+      for (int gi = 0; gi < GI; ++gi)
+#pragma unroll
+        for (int t = 0; t < TPW; ++t)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[gi][t][i] = kMagicBits;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int gi = 0; gi < GI; ++gi)
+#pragma unroll
+          for (int t = 0; t < TPW; ++t)
+            mma_s8_16832(acc[gi][t], aw[gi][q][0], aw[gi][q][1], aw[gi][q][2], aw[gi][q][3], bq[gi][t][2 * q],
+                         bq[gi][t][2 * q + 1]);
+      // acc reads as F = 12582912 + S*dot, S = 16 (A8: codes x 16-weights) or 256
+      constexpr float kInvS = A8 ? 0.0625f : 0.00390625f;
+      constexpr float kOff = A8 ? -786432.0f : -49152.0f;
+#pragma unroll
+      for (int gi = 0; gi < GI; ++gi) {   // groups in increasing order
+        const int g = it * 2 + gb + gi;
+        if (g >= G) break;
+        float sw0 = 1.0f, sw1 = 1.0f;
+        if (WG) {
+          sw0 = bf16_bits_to_f32(sw_s[row_lo * G + g]);
+          sw1 = bf16_bits_to_f32(sw_s[row_hi * G + g]);
+        }
+        const bool fast = A8 && fast_g[g] != 0;
+#pragma unroll
+        for (int t = 0; t < TPW; ++t) {
+          const int* a = acc[gi][t];
+          const int tok = (tile0 + t) * 8 + tig * 2;
+          if (fast) {
+            const float4 c = *reinterpret_cast<const float4*>(&sac[g * MP + tok]);  // (sa0/16, c0, sa1/16, c1)
+            const float ds0 = fmaf(__int_as_float(a[0]), c.x, c.y);
+            const float ds1 = fmaf(__int_as_float(a[1]), c.z, c.w);
+            const float ds2 = fmaf(__int_as_float(a[2]), c.x, c.y);
+            const float ds3 = fmaf(__int_as_float(a[3]), c.z, c.w);
+            if (WG) {
+              tot[t][0] = fmaf(ds0, sw0, tot[t][0]);
+              tot[t][1] = fmaf(ds1, sw0, tot[t][1]);
+              tot[t][2] = fmaf(ds2, sw1, tot[t][2]);
+              tot[t][3] = fmaf(ds3, sw1, tot[t][3]);
+            } else {
+              tot[t][0] = __fadd_rn(tot[t][0], ds0);
+              tot[t][1] = __fadd_rn(tot[t][1], ds1);
+              tot[t][2] = __fadd_rn(tot[t][2], ds2);
+              tot[t][3] = __fadd_rn(tot[t][3], ds3);
+            }
           } else {
-            tot[si][tt][0] = fmaf(d0, sa0[tt], tot[si][tt][0]);
-            tot[si][tt][1] = fmaf(d1, sa1[tt], tot[si][tt][1]);
-            tot[si][tt][2] = fmaf(d2, sa0[tt], tot[si][tt][2]);
-            tot[si][tt][3] = fmaf(d3, sa1[tt], tot[si][tt][3]);
+            const float sa0 = bf16_bits_to_f32(sa_s[tok * G + g]);
+            const float sa1 = bf16_bits_to_f32(sa_s[(tok + 1) * G + g]);
+            const float d0 = fmaf(__int_as_float(a[0]), kInvS, kOff);
+            const float d1 = fmaf(__int_as_float(a[1]), kInvS, kOff);
+            const float d2 = fmaf(__int_as_float(a[2]), kInvS, kOff);
+            const float d3 = fmaf(__int_as_float(a[3]), kInvS, kOff);
+            if (WG) {
+              tot[t][0] = fmaf(d0, __fmul_rn(sa0, sw0), tot[t][0]);
+              tot[t][1] = fmaf(d1, __fmul_rn(sa1, sw0), tot[t][1]);
+              tot[t][2] = fmaf(d2, __fmul_rn(sa0, sw1), tot[t][2]);
+              tot[t][3] = fmaf(d3, __fmul_rn(sa1, sw1), tot[t][3]);
+            } else {
+              tot[t][0] = fmaf(d0, sa0, tot[t][0]);
+              tot[t][1] = fmaf(d1, sa1, tot[t][1]);
+              tot[t][2] = fmaf(d2, sa0, tot[t][2]);
+              tot[t][3] = fmaf(d3, sa1, tot[t][3]);
+            }
           }
         }
       }
@@ -216,36 +372,31 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     return;
   }
 
+  const int r0 = n0 + row_lo, r1 = n0 + row_hi;
+  float swc0 = 1.0f, swc1 = 1.0f;
+  if (!WG) {
+    swc0 = bf16_bits_to_f32(sw_s[row_lo]);
+    swc1 = bf16_bits_to_f32(sw_s[row_hi]);
+  }
 #pragma unroll
-  for (int si = 0; si < kMaxSlabsPerWarp; ++si) {
-    const int slab = cw + kConsumerWarps * si;
-    if (slab >= nslab) break;
-    const int r0 = n0 + slab * 16 + gid, r1 = r0 + 8;
-    float swc0 = 1.0f, swc1 = 1.0f;
-    if (!WGROUPED) {
-      swc0 = bf16_bits_to_f32(sw_s[slab * 16 + gid]);
-      swc1 = bf16_bits_to_f32(sw_s[slab * 16 + gid + 8]);
+  for (int t = 0; t < TPW; ++t) {
+    const int t0 = m0 + (tile0 + t) * 8 + tig * 2, t1 = t0 + 1;
+    float v[4] = {tot[t][0], tot[t][1], tot[t][2], tot[t][3]};
+    if (!WG) {
+      v[0] = __fmul_rn(v[0], swc0);
+      v[1] = __fmul_rn(v[1], swc0);
+      v[2] = __fmul_rn(v[2], swc1);
+      v[3] = __fmul_rn(v[3], swc1);
     }
+    const int rr[4] = {r0, r0, r1, r1}, tk[4] = {t0, t1, t0, t1};
 #pragma unroll
-    for (int tt = 0; tt < MT; ++tt) {
-      const int t0 = m0 + tt * 8 + tig * 2, t1 = t0 + 1;
-      float v[4] = {tot[si][tt][0], tot[si][tt][1], tot[si][tt][2], tot[si][tt][3]};
-      if (!WGROUPED) {
-        v[0] = __fmul_rn(v[0], swc0);
-        v[1] = __fmul_rn(v[1], swc0);
-        v[2] = __fmul_rn(v[2], swc1);
-        v[3] = __fmul_rn(v[3], swc1);
-      }
-      const int rr[4] = {r0, r0, r1, r1}, tk[4] = {t0, t1, t0, t1};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        if (tk[i] < p.M && rr[i] < p.N) {
-          const size_t o = static_cast<size_t>(tk[i]) * p.N + rr[i];
-          if (OUT_F32)
-            static_cast<float*>(p.out)[o] = v[i];
-          else
-            static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(v[i]);
-        }
+    for (int i = 0; i < 4; ++i) {
+      if (tk[i] < p.M && rr[i] < p.N) {
+        const size_t o = static_cast<size_t>(tk[i]) * p.N + rr[i];
+        if (F32)
+          static_cast<float*>(p.out)[o] = v[i];
+        else
+          static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(v[i]);
       }
     }
   }
@@ -274,52 +425,92 @@ __global__ void w4a4_group_dots_kernel(const uint8_t* __restrict__ a, const uint
 }
 
 // ------------------------------------------------------------ host side
-template <int MT, bool WG, bool F32>
-static int launch_stream_t(const CUtensorMap& tw, const CUtensorMap& ta, const StreamGemmArgs& a, dim3 grid,
-                           int smem, cudaStream_t stream) {
+template <int MT, int TPW, bool A8, bool WG, bool F32>
+static int launch_t(const CUtensorMap* maps, const StreamGemmArgs& a, dim3 grid, int threads, int smem,
+                    cudaStream_t stream) {
   static int done[64] = {};
-  const int rc = ensure_smem_attr(reinterpret_cast<const void*>(&w4a4_stream_kernel<MT, WG, F32>), smem, done);
+  auto* kern = &w4a4_stream_kernel<MT, TPW, A8, WG, F32>;
+  const int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem, done);
   if (rc != NV4_OK) return rc;
-  return launch_kernel(w4a4_stream_kernel<MT, WG, F32>, grid, dim3(kStreamThreads), smem, stream, true, tw, ta, a);
+  return launch_kernel(kern, grid, dim3(threads), smem, stream, true, maps[0], maps[1], maps[2], maps[3], a);
 }
 
-template <int MT>
-static int launch_stream_mt(const CUtensorMap& tw, const CUtensorMap& ta, const StreamGemmArgs& a, dim3 grid,
-                            int smem, bool wg, bool f32, cudaStream_t stream) {
-  if (wg) return f32 ? launch_stream_t<MT, true, true>(tw, ta, a, grid, smem, stream)
-                     : launch_stream_t<MT, true, false>(tw, ta, a, grid, smem, stream);
-  return f32 ? launch_stream_t<MT, false, true>(tw, ta, a, grid, smem, stream)
-             : launch_stream_t<MT, false, false>(tw, ta, a, grid, smem, stream);
+template <int MT, int TPW>
+static int launch_flags(const CUtensorMap* maps, const StreamGemmArgs& a, dim3 grid, int threads, int smem, bool a8,
+                        bool wg, bool f32, cudaStream_t s) {
+  if (a8) {
+    if (wg) return f32 ? launch_t<MT, TPW, true, true, true>(maps, a, grid, threads, smem, s)
+                       : launch_t<MT, TPW, true, true, false>(maps, a, grid, threads, smem, s);
+    return f32 ? launch_t<MT, TPW, true, false, true>(maps, a, grid, threads, smem, s)
+               : launch_t<MT, TPW, true, false, false>(maps, a, grid, threads, smem, s);
+  }
+  if (wg) return f32 ? launch_t<MT, TPW, false, true, true>(maps, a, grid, threads, smem, s)
+                     : launch_t<MT, TPW, false, true, false>(maps, a, grid, threads, smem, s);
+  return f32 ? launch_t<MT, TPW, false, false, true>(maps, a, grid, threads, smem, s)
+             : launch_t<MT, TPW, false, false, false>(maps, a, grid, threads, smem, s);
 }
 
 constexpr int kSmemLimit = 227 * 1024;
 
-int launch_w4a4_stream_gemm(const void* a_packed, const void* w_packed, const void* a_scale, const void* w_scale,
-                            void* out, int64_t m, int64_t n, int64_t k, int flags, cudaStream_t stream) {
+static bool make_map_u16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows,
+                         uint32_t box_cols) {
+  return make_tensor_map_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, base, rows, cols, box_rows, box_cols,
+                            CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+// a8 != nullptr: activations in the widened INT8 layout [m, k]; else a_packed [m, k/2].
+int launch_w4a4_stream_gemm(const void* a_packed, const void* a8, const void* w_packed, const void* a_scale,
+                            const void* w_scale, void* out, int64_t m, int64_t n, int64_t k, int flags,
+                            cudaStream_t stream) {
   const int sms = device_sm_count();
   if (sms <= 0) return NV4_ERR_CUDA;
   const bool wg = (flags & NV4_GEMM_W_SCALE_GROUPED) != 0;
   const bool f32 = (flags & NV4_GEMM_OUT_FP32) != 0;
+  const bool use_a8 = a8 != nullptr;
   const int MT = m <= 8 ? 1 : (m <= 16 ? 2 : 4);
   const int MP = MT * 8;
   const int64_t mblocks = (m + MP - 1) / MP;
   const int G = static_cast<int>(k / 128);
-  // About one CTA per SM: rows per CTA, rounded up to whole 16-row slabs.
+  const int64_t total_slabs = (n + 15) / 16;
+  // About one CTA per SM: slabs (16-row units) per CTA.
   const int64_t ctas_per_mblock = std::max<int64_t>(1, sms / std::min<int64_t>(mblocks, sms));
-  int64_t R = (n + ctas_per_mblock - 1) / ctas_per_mblock;
-  R = std::min<int64_t>(256, std::max<int64_t>(16, (R + 15) / 16 * 16));
-  const int scale_bytes = (wg ? G * static_cast<int>(R) : static_cast<int>(R)) * 2 + 16 + G * MP * 4 + 16;
-  const int stage_bytes = static_cast<int>(R + MP) * 128;
+  int slabs = static_cast<int>(std::min<int64_t>(kMaxConsumerWarps, (total_slabs + ctas_per_mblock - 1) / ctas_per_mblock));
+  slabs = std::max(1, slabs);
+  // Narrow layers: split token tiles over two warps per slab (each widens the
+  // slab's weights, so no further) when there are few slabs per CTA.
+  int ts = 1;
+  if (MT >= 2 && slabs * 2 <= kMaxConsumerWarps && slabs < 8) ts = 2;
+  const int tpw = MT / ts;
+  const int R = slabs * 16;
   const int n_iters = (G + 1) / 2;
-  int stages = (kSmemLimit - 1024 - scale_bytes - 64) / (stage_bytes + 16);
-  stages = std::min(stages, std::min(8, n_iters));
+  const bool scale_tma = (G % 8) == 0 && (reinterpret_cast<uintptr_t>(a_scale) & 15) == 0 &&
+                         (reinterpret_cast<uintptr_t>(w_scale) & 15) == 0;
+  const StreamLayout one(R, MP, G, 1, wg);
+  const int fixed = one.total - one.stage_bytes;
+  int stages = (kSmemLimit - 1024 - fixed - 64) / (one.stage_bytes + 16);
+  stages = std::min(stages, std::min(16, n_iters));
   if (stages < 1) return NV4_ERR_UNSUPPORTED;
-  const int smem = 1024 + stages * (stage_bytes + 16) + 16 + scale_bytes + 64;
+  const StreamLayout lay(R, MP, G, stages, wg);
+  const int smem = lay.total + 1024;
 
-  CUtensorMap tw, ta;
-  if (!make_tensor_map_u8(&tw, w_packed, n, k / 2, static_cast<uint32_t>(R), 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_tensor_map_u8(&ta, a_packed, m, k / 2, static_cast<uint32_t>(MP), 128, CU_TENSOR_MAP_SWIZZLE_128B))
-    return NV4_ERR_CUDA;
+  CUtensorMap maps[4];
+  memset(maps, 0, sizeof(maps));
+  bool okm = make_tensor_map_u8(&maps[0], w_packed, n, k / 2, static_cast<uint32_t>(R), 128,
+                                CU_TENSOR_MAP_SWIZZLE_128B);
+  if (use_a8)
+    okm = okm && make_tensor_map_u8(&maps[1], a8, m, k, static_cast<uint32_t>(MP), 128, CU_TENSOR_MAP_SWIZZLE_128B);
+  else
+    okm = okm && make_tensor_map_u8(&maps[1], a_packed, m, k / 2, static_cast<uint32_t>(MP), 128,
+                                    CU_TENSOR_MAP_SWIZZLE_128B);
+  if (scale_tma) {
+    if (wg)
+      okm = okm && make_map_u16(&maps[2], w_scale, n, G, static_cast<uint32_t>(R), G);
+    else
+      okm = okm && make_map_u16(&maps[2], w_scale, 1, n, 1, static_cast<uint32_t>(R));
+    okm = okm && make_map_u16(&maps[3], a_scale, m, G, static_cast<uint32_t>(MP), G);
+  }
+  if (!okm) return NV4_ERR_CUDA;
+
   StreamGemmArgs a;
   a.a_scale = static_cast<const uint16_t*>(a_scale);
   a.w_scale = static_cast<const uint16_t*>(w_scale);
@@ -327,13 +518,22 @@ int launch_w4a4_stream_gemm(const void* a_packed, const void* w_packed, const vo
   a.M = static_cast<int>(m);
   a.N = static_cast<int>(n);
   a.G = G;
-  a.R = static_cast<int>(R);
+  a.R = R;
+  a.slabs = slabs;
   a.n_iters = n_iters;
   a.stages = stages;
+  a.scale_tma = scale_tma ? 1 : 0;
   const dim3 grid(static_cast<unsigned>((n + R - 1) / R), static_cast<unsigned>(mblocks));
-  if (MT == 1) return launch_stream_mt<1>(tw, ta, a, grid, smem, wg, f32, stream);
-  if (MT == 2) return launch_stream_mt<2>(tw, ta, a, grid, smem, wg, f32, stream);
-  return launch_stream_mt<4>(tw, ta, a, grid, smem, wg, f32, stream);
+  const int threads = 32 * (1 + slabs * ts);
+  switch (MT * 10 + tpw) {
+    case 11: return launch_flags<1, 1>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
+    case 21: return launch_flags<2, 1>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
+    case 22: return launch_flags<2, 2>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
+    case 41: return launch_flags<4, 1>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
+    case 42: return launch_flags<4, 2>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
+    case 44: return launch_flags<4, 4>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
+    default: return NV4_ERR_UNSUPPORTED;
+  }
 }
 
 int launch_w4a4_group_dots(const void* a_packed, const void* w_packed, int32_t* dots, int64_t m, int64_t n, int64_t k,

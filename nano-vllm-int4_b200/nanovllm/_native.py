@@ -32,7 +32,7 @@ GEMM_W_SCALE_GROUPED = 1
 GEMM_OUT_FP32 = 2
 GEMM_FORCE_STREAM = 4
 
-EXPORTS = ("nv4_rht_quant_pack", "nv4_w4a4_grouped_gemm", "nv4_w4a4_group_dots", "nv4_w4a16_gemm",
+EXPORTS = ("nv4_rht_quant_pack", "nv4_rht_quant_i8", "nv4_w4a4_grouped_gemm", "nv4_w4a4_gemm_i8", "nv4_w4a4_group_dots", "nv4_w4a16_gemm",
            "nv4_w4a16_workspace_bytes", "nv4_version", "nv4_status_string", "nv4_last_cuda_error",
            "nv4_device_error")
 
@@ -54,6 +54,25 @@ _lock = threading.Lock()
 _vp, _i64, _int = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
 
 
+def _check_fresh(path: str) -> None:
+    """Refuse a library built from other sources than the ones beside it (when
+    the sources are present): a stale binary would silently run old kernels."""
+    pkg = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    builder = os.path.join(pkg, "build_native.py")
+    stamp = path + ".srchash"
+    if not os.path.exists(builder) or not os.path.isdir(os.path.join(pkg, "csrc")):
+        return
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("_nv4_build_native", builder)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    recorded = open(stamp).read().strip() if os.path.exists(stamp) else ""
+    if recorded != mod.source_hash():
+        raise NativeLibraryError(
+            f"{path} was not built from the current sources; rebuild with "
+            f"`python nano-vllm-int4_b200/build_native.py`")
+
+
 def load(path: str | None = None) -> ctypes.CDLL:
     """Load libnv4.so once (raises NativeLibraryError when it is absent)."""
     global _lib
@@ -66,12 +85,16 @@ def load(path: str | None = None) -> ctypes.CDLL:
         if not os.path.exists(p):
             raise NativeLibraryError(
                 f"libnv4.so not found at {p}; build it with `python nano-vllm-int4_b200/build_native.py`")
+        if path is None:
+            _check_fresh(p)
         try:
             lib = ctypes.CDLL(p)
         except OSError as e:  # pragma: no cover - depends on the host
             raise NativeLibraryError(f"failed to load {p}: {e}") from e
         lib.nv4_rht_quant_pack.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _int, _int, _vp]
+        lib.nv4_rht_quant_i8.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _int, _int, _vp]
         lib.nv4_w4a4_grouped_gemm.argtypes = [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]
+        lib.nv4_w4a4_gemm_i8.argtypes = [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]
         lib.nv4_w4a4_group_dots.argtypes = [_vp, _vp, _vp, _i64, _i64, _i64, _vp]
         lib.nv4_w4a16_gemm.argtypes = [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _vp]
         lib.nv4_w4a16_workspace_bytes.argtypes = [_i64, _i64, _i64]
@@ -79,7 +102,7 @@ def load(path: str | None = None) -> ctypes.CDLL:
         lib.nv4_status_string.argtypes = [_int]
         lib.nv4_status_string.restype = ctypes.c_char_p
         lib.nv4_device_error.argtypes = [ctypes.POINTER(_int)]
-        for name in ("nv4_rht_quant_pack", "nv4_w4a4_grouped_gemm", "nv4_w4a4_group_dots", "nv4_w4a16_gemm",
+        for name in ("nv4_rht_quant_pack", "nv4_rht_quant_i8", "nv4_w4a4_grouped_gemm", "nv4_w4a4_gemm_i8", "nv4_w4a4_group_dots", "nv4_w4a16_gemm",
                      "nv4_version", "nv4_last_cuda_error", "nv4_device_error"):
             getattr(lib, name).restype = _int
         if path is None:
@@ -119,6 +142,20 @@ def rht_quant_pack(x, signs, packed, scale, layout: int, clamp_lo: int) -> None:
     with torch.cuda.device(x.device):
         check(load().nv4_rht_quant_pack(ptr(x), ptr(signs), ptr(packed), ptr(scale), m, k, layout, clamp_lo,
                                         stream_of(x)), "nv4_rht_quant_pack")
+
+
+def rht_quant_i8(x, signs, codes, scale, layout: int, clamp_lo: int) -> None:
+    m, k = x.shape
+    with torch.cuda.device(x.device):
+        check(load().nv4_rht_quant_i8(ptr(x), ptr(signs), ptr(codes), ptr(scale), m, k, layout, clamp_lo,
+                                      stream_of(x)), "nv4_rht_quant_i8")
+
+
+def w4a4_gemm_i8(a_codes, w_packed, a_scale, w_scale, out, flags: int) -> None:
+    m, k, n = a_codes.shape[0], a_codes.shape[1], w_packed.shape[0]
+    with torch.cuda.device(a_codes.device):
+        check(load().nv4_w4a4_gemm_i8(ptr(a_codes), ptr(w_packed), ptr(a_scale), ptr(w_scale), ptr(out),
+                                      m, n, k, flags, stream_of(a_codes)), "nv4_w4a4_gemm_i8")
 
 
 def w4a4_grouped_gemm(a_packed, w_packed, a_scale, w_scale, out, flags: int) -> None:

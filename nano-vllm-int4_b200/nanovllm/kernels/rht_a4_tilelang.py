@@ -90,3 +90,34 @@ def rht_quant_pack(x, signs, *, out_packed, out_scale, config=None, layout=LAYOU
         _check_config(config)
     _native.rht_quant_pack(x, signs, out_packed, out_scale, lid, clamp_lo)
     return out_packed, out_scale
+
+
+def rht_quant_i8(x, signs, *, out_codes, out_scale, layout=LAYOUT_VERSION, clamp_lo=-7):
+    """Same transform and quantisation as ``rht_quant_pack``, with the codes
+    written as GEMM-ready INT8 ``out_codes`` [M, K] (each 32-wide K chunk holds
+    its 16 even-k codes, then its 16 odd-k codes) for ``w4a4_grouped_gemm_i8``."""
+    lid = _layout_id(layout)
+    if x.ndim != 2 or x.dtype != torch.bfloat16 or x.shape[0] < 1:
+        raise ValueError('Expected BF16 X[M,K], M>0')
+    m, k = x.shape
+    if (lid == _native.LAYOUT_ROW_DH and k not in (4096, 12288)) or k % 128 or k < 128:
+        raise ValueError('Unsupported K for this layout')
+    if signs.shape != (k,) or signs.dtype != torch.int8:
+        raise ValueError('Expected INT8 signs[K]')
+    if out_codes.shape != (m, k) or out_codes.dtype != torch.int8:
+        raise ValueError('Expected INT8 codes[M,K]')
+    if out_scale.shape != (m, k // 128) or out_scale.dtype != torch.bfloat16:
+        raise ValueError('Expected BF16 scales[M,K/128]')
+    if any(not t.is_cuda or not t.is_contiguous() or t.device != x.device for t in [x, signs, out_codes, out_scale]):
+        raise ValueError('All tensors must be contiguous on one CUDA device')
+    if clamp_lo not in (-7, -8):
+        raise ValueError('clamp_lo must be -7 or -8')
+    _native.rht_quant_i8(x, signs, out_codes, out_scale, lid, clamp_lo)
+    return out_codes, out_scale
+
+
+def i8_to_codes(codes_i8: torch.Tensor) -> torch.Tensor:
+    """Undo the GEMM-ready K order of ``rht_quant_i8`` (for checks): [M, K] codes in k order."""
+    m, k = codes_i8.shape
+    c = codes_i8.reshape(m, k // 32, 2, 16)          # [chunk][even/odd][i]
+    return c.permute(0, 1, 3, 2).reshape(m, k)        # k = 2i + parity

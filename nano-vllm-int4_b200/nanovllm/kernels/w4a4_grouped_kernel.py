@@ -105,6 +105,39 @@ def w4a4_grouped_gemm(a_packed, w_packed, a_scale, w_scale, out=None, config=Non
     return out
 
 
+def w4a4_grouped_gemm_i8(a_codes, w_packed, a_scale, w_scale, out=None, *, out_fp32=False, force_stream=False):
+    """``w4a4_grouped_gemm`` with activations as the INT8 [M, K] codes written by
+    ``rht_quant_i8`` (same results; used by the linear layers).  More than 64
+    tokens run on the tcgen05 kernel, fewer on the mma.sync weight-streaming
+    kernel; ``force_stream=True`` selects the latter for any size."""
+    if a_codes.ndim != 2 or w_packed.ndim != 2 or a_codes.shape[1] != w_packed.shape[1] * 2:
+        raise ValueError("Require INT8 codes [M,K] and packed weights [N,K/2]")
+    if a_codes.dtype != torch.int8 or w_packed.dtype != torch.int8:
+        raise TypeError("Codes and packed weights must use int8 storage")
+    M, K, N = a_codes.shape[0], a_codes.shape[1], w_packed.shape[0]
+    if K % GROUP_SIZE or N % 8 or min(M, N, K) < 1:
+        raise ValueError("Require positive dimensions, K divisible by 128, N divisible by 8")
+    weight_grouped = w_scale.ndim == 2
+    expected_w_scale = (N, K // GROUP_SIZE) if weight_grouped else (N,)
+    if a_scale.shape != (M, K // GROUP_SIZE) or w_scale.shape != expected_w_scale:
+        raise ValueError("Require Sa[M,K/128] and Sw[N] or Sw[N,K/128]")
+    if a_scale.dtype != torch.bfloat16 or w_scale.dtype != torch.bfloat16:
+        raise TypeError("Both scale tensors must be BF16")
+    tensors = (a_codes, w_packed, a_scale, w_scale)
+    if any(not t.is_cuda or not t.is_contiguous() or t.device != a_codes.device for t in tensors):
+        raise ValueError("All inputs must be contiguous CUDA tensors on one device")
+    dtype = torch.float32 if out_fp32 else torch.bfloat16
+    if out is None:
+        out = torch.empty((M, N), device=a_codes.device, dtype=dtype)
+    if out.shape != (M, N) or out.dtype != dtype or out.device != a_codes.device or not out.is_contiguous():
+        raise ValueError("Output must be contiguous [M,N] on the input device")
+    flags = (_native.GEMM_W_SCALE_GROUPED if weight_grouped else 0) | (_native.GEMM_OUT_FP32 if out_fp32 else 0)
+    if force_stream:
+        flags |= _native.GEMM_FORCE_STREAM
+    _native.w4a4_gemm_i8(a_codes, w_packed, a_scale, w_scale, out, flags)
+    return out
+
+
 def w4a4_group_dots(a_packed, w_packed):
     """Exact per-group INT32 dot products [K/128, M, N] (diagnostic)."""
     if a_packed.ndim != 2 or w_packed.ndim != 2 or a_packed.shape[1] != w_packed.shape[1]:

@@ -30,8 +30,8 @@ import torch
 import torch.distributed as dist
 from torch import nn
 
-from nanovllm.kernels.rht_a4_tilelang import LAYOUT_VERSION, rht_quant_pack
-from nanovllm.kernels.w4a4_grouped_kernel import w4a4_grouped_gemm
+from nanovllm.kernels.rht_a4_tilelang import LAYOUT_VERSION, rht_quant_i8
+from nanovllm.kernels.w4a4_grouped_kernel import w4a4_grouped_gemm_i8
 from nanovllm import _native
 
 BLOCK128 = "block128"
@@ -74,19 +74,20 @@ class W4A4Linear(nn.Module):
         self.register_buffer("signs", torch.empty(input_size, dtype=torch.int8))
 
     def quantize_input(self, flat: torch.Tensor):
+        """Activation prep into the GEMM-ready INT8 layout: (codes [M,K], scales [M,K/128])."""
         m, k = flat.shape
-        packed = torch.empty((m, k // 2), dtype=torch.int8, device=flat.device)
+        codes = torch.empty((m, k), dtype=torch.int8, device=flat.device)
         scale = torch.empty((m, k // 128), dtype=torch.bfloat16, device=flat.device)
-        rht_quant_pack(flat, self.signs, out_packed=packed, out_scale=scale, layout=self.layout_id,
-                       clamp_lo=self.clamp_lo)
-        return packed, scale
+        rht_quant_i8(flat, self.signs, out_codes=codes, out_scale=scale, layout=self.layout_id,
+                     clamp_lo=self.clamp_lo)
+        return codes, scale
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if x.shape[-1] != self.in_features or x.dtype != torch.bfloat16:
             raise ValueError("W4A4Linear requires BF16 activations with the configured input width")
         flat = x.reshape(-1, self.in_features).contiguous()
-        packed, scale = self.quantize_input(flat)
-        out = w4a4_grouped_gemm(packed, self.packed_weight, scale, self.weight_scale)
+        codes, scale = self.quantize_input(flat)
+        out = w4a4_grouped_gemm_i8(codes, self.packed_weight, scale, self.weight_scale)
         return out.reshape(*x.shape[:-1], self.out_features)
 
     @torch.no_grad()
@@ -216,16 +217,16 @@ class W4A4RowParallelLinear(W4A4Linear):
             parts = [torch.empty_like(flat) for _ in range(self.tp_size)]
             dist.all_gather(parts, flat, group=self.group)
             full = torch.cat(parts, dim=1)
-            packed_full, scale_full = W4A4Linear.quantize_input(self, full)
+            codes_full, scale_full = W4A4Linear.quantize_input(self, full)
             k_local = self.in_features
-            packed = packed_full[:, self.tp_rank * k_local // 2:(self.tp_rank + 1) * k_local // 2].contiguous()
+            codes = codes_full[:, self.tp_rank * k_local:(self.tp_rank + 1) * k_local].contiguous()
             scale = scale_full[:, self.tp_rank * k_local // 128:(self.tp_rank + 1) * k_local // 128].contiguous()
         else:
-            packed, scale = self.quantize_input(flat)
+            codes, scale = self.quantize_input(flat)
         if self.tp_size == 1:
-            out = w4a4_grouped_gemm(packed, self.packed_weight, scale, self.weight_scale)
+            out = w4a4_grouped_gemm_i8(codes, self.packed_weight, scale, self.weight_scale)
         else:
-            partial = w4a4_grouped_gemm(packed, self.packed_weight, scale, self.weight_scale, out_fp32=True)
+            partial = w4a4_grouped_gemm_i8(codes, self.packed_weight, scale, self.weight_scale, out_fp32=True)
             dist.all_reduce(partial, group=self.group)
             out = partial.to(torch.bfloat16)
         return out.reshape(*x.shape[:-1], self.out_features)

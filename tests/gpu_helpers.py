@@ -29,3 +29,10 @@ class Guarded:
 
 def bf16_bits_to_float(bits: np.ndarray) -> np.ndarray:
     return (bits.astype(np.uint32) << 16).view(np.float32)
+
+
+def codes_to_i8_layout(codes: torch.Tensor) -> torch.Tensor:
+    """int8 codes [M, K] in k order -> the GEMM-ready layout of nv4_rht_quant_i8:
+    within each 32-wide K chunk, the 16 even-k codes then the 16 odd-k codes."""
+    m, k = codes.shape
+    return codes.reshape(m, k // 32, 16, 2).permute(0, 1, 3, 2).reshape(m, k).contiguous()

@@ -130,3 +130,51 @@ def test_extreme_scales(cuda_device):
     d = cuda_device
     got32 = run_gemm(pack(qa).to(d), pack(qw).to(d), sa.to(d), sw.to(d), fp32=True)
     np.testing.assert_array_equal(got32.numpy(), oracle_out(qa, qw, sa, sw))
+
+
+@pytest.mark.parametrize("force_stream", [False, True], ids=["tcgen05", "mma_sync"])
+@pytest.mark.parametrize("grouped", [True, False])
+@pytest.mark.parametrize("m,n,k", [(1, 6144, 4096), (8, 4096, 4096), (32, 24576, 4096), (32, 4096, 12288),
+                                   (17, 96, 512), (33, 136, 4096), (100, 64, 2048), (5, 24, 384),
+                                   (128, 256, 4096), (300, 512, 1024), (1024, 384, 12288)])
+def test_i8_activation_gemm_exact(cuda_device, m, n, k, grouped, force_stream):
+    """nv4_w4a4_gemm_i8 (the path W4A4Linear uses) equals the oracle bit for bit,
+    on the tcgen05 kernel and on the mma.sync kernel."""
+    from gpu_helpers import codes_to_i8_layout
+    g = torch.Generator().manual_seed(m * 7 + n + k)
+    qa = torch.randint(-8, 8, (m, k), generator=g, dtype=torch.int8)
+    qw = torch.randint(-8, 8, (n, k), generator=g, dtype=torch.int8)
+    sa = (torch.rand(m, k // 128, generator=g) * 2).bfloat16()
+    sw = ((torch.rand(n, k // 128, generator=g) if grouped else torch.rand(n, generator=g)) * .03).bfloat16()
+    d = cuda_device
+    a8 = codes_to_i8_layout(qa).to(d)
+    for fp32 in (False, True):
+        out = Guarded((m, n), torch.float32 if fp32 else torch.bfloat16, d, -1234.0, float("nan"))
+        wk.w4a4_grouped_gemm_i8(a8, pack(qw).to(d), sa.to(d), sw.to(d), out=out.view, out_fp32=fp32,
+                                force_stream=force_stream)
+        torch.cuda.synchronize()
+        assert out.intact()
+        ref = oracle_out(qa, qw, sa, sw)
+        if fp32:
+            np.testing.assert_array_equal(out.view.cpu().numpy(), ref)
+        else:
+            np.testing.assert_array_equal(u16(out.view), o.f32_to_bf16_bits(ref))
+    assert _native.device_error() == 0
+
+
+def test_i8_gemm_extreme_scales_use_exact_path(cuda_device):
+    """Scales outside the two-FMA fast range take the reference's three-step form."""
+    from gpu_helpers import codes_to_i8_layout
+    m, n, k = 16, 64, 1024
+    g = torch.Generator().manual_seed(9)
+    qa = torch.randint(-8, 8, (m, k), generator=g, dtype=torch.int8)
+    qw = torch.randint(-8, 8, (n, k), generator=g, dtype=torch.int8)
+    exps = torch.tensor([-126, -110, -60, -20, 0, 20, 60, 105], dtype=torch.float32)
+    sa = torch.ldexp(torch.rand(m, k // 128, generator=g) + 1,
+                     exps[torch.arange(m * (k // 128)) % 8].reshape(m, -1)).bfloat16()
+    sw = (torch.rand(n, k // 128, generator=g) * .03).bfloat16()
+    sw[3, 2] = 2.0 ** -120
+    d = cuda_device
+    got = wk.w4a4_grouped_gemm_i8(codes_to_i8_layout(qa).to(d), pack(qw).to(d), sa.to(d), sw.to(d),
+                                  out_fp32=True).cpu().numpy()
+    np.testing.assert_array_equal(got, oracle_out(qa, qw, sa, sw))

@@ -101,12 +101,12 @@ def test_tp_shards_single_gpu(cuda_device, tp):
     ref_r = full_r(xr).float()
     total = torch.zeros(32, nr, device=cuda_device)
     kl = kr // tp
-    from nanovllm.kernels.w4a4_grouped_kernel import w4a4_grouped_gemm
+    from nanovllm.kernels.w4a4_grouped_kernel import w4a4_grouped_gemm_i8
     for r in range(tp):
         row = W4A4RowParallelLinear(kr, nr, tp_rank=r, tp_size=tp).to(cuda_device)
         row.load_full(packed_r.to(cuda_device), scale_r.to(cuda_device), signs_r.to(cuda_device))
-        p, s = row.quantize_input(xr[:, r * kl:(r + 1) * kl].contiguous())
-        total += w4a4_grouped_gemm(p, row.packed_weight, s, row.weight_scale, out_fp32=True)
+        c, s = row.quantize_input(xr[:, r * kl:(r + 1) * kl].contiguous())
+        total += w4a4_grouped_gemm_i8(c, row.packed_weight, s, row.weight_scale, out_fp32=True)
     got = total.bfloat16().float()
     rel = (got - ref_r).norm() / ref_r.norm()
     assert rel < 1e-3

@@ -20,7 +20,7 @@ def declared_symbols():
 def test_library_exports_every_declared_symbol():
     lib = _native.load()
     names = declared_symbols()
-    assert len(names) >= 9
+    assert len(names) >= 11
     for name in names:
         assert hasattr(lib, name), name
     assert set(names) == set(_native.EXPORTS)

@@ -131,3 +131,24 @@ def test_stream_and_graph_replay(cuda_device, layout, k):
         graph.replay()
         torch.cuda.synchronize()
         assert_matches_oracle(x.cpu(), signs.cpu(), u8(packed), u16(scale), layout, lo)
+
+
+@pytest.mark.parametrize("layout,lo,k,m", [("block128", -8, 4096, 33), ("block128", -7, 12288, 7),
+                                           ("row_DH", -7, 4096, 17), ("row_DH", -7, 12288, 5),
+                                           ("block128", -8, 4096, 4097)])
+def test_i8_layout_matches_oracle(cuda_device, layout, lo, k, m):
+    """nv4_rht_quant_i8: same codes and scales as the packed form, in the GEMM-ready K order."""
+    from nanovllm.kernels.rht_a4_tilelang import i8_to_codes, rht_quant_i8
+    x = synthetic.activations(m, k, seed=m + k)
+    x[: min(m, 6)] = synthetic.make_input(min(m, 6), k)
+    signs = synthetic.make_signs(k, 5)
+    d = cuda_device
+    codes = Guarded((m, k), torch.int8, d, -69, 85)
+    scale = Guarded((m, k // 128), torch.bfloat16, d, -17.0, float("nan"))
+    rht_quant_i8(x.to(d), signs.to(d), out_codes=codes.view, out_scale=scale.view, layout=layout, clamp_lo=lo)
+    torch.cuda.synchronize()
+    assert codes.intact() and scale.intact()
+    _, ref_sbits, ref_codes, _, _ = o.prepare(u16(x), signs.numpy(), LAYOUTS[layout], lo)
+    got = i8_to_codes(codes.view.cpu()).numpy()
+    assert int((got != ref_codes).sum()) == 0
+    np.testing.assert_array_equal(u16(scale.view), ref_sbits)
