@@ -123,6 +123,33 @@ int nv4_w4a16_gemm(const void* x, const void* qweight, const void* qzeros, const
                    void* stream);
 int64_t nv4_w4a16_workspace_bytes(int64_t m, int64_t n, int64_t k);
 
+/*
+ * nv4_w4a16_gemm without a workspace argument (no counterpart in the
+ * reference, whose kernel adds into a pre-zeroed output instead).  Same
+ * arguments, requirements and results as nv4_w4a16_gemm.
+ *
+ * Meant for callers that cannot hand out device memory at call time: a host
+ * runtime that reserved all of HBM at start-up for its page pool and weights,
+ * or a plain C caller with no device allocator of its own.  The call
+ * allocates nothing: the split-K partial sums of small m go to a 2 MiB float32
+ * array compiled into the library (one per device).
+ *
+ *   - Limit: when m <= 16 (the split-K case), m * n must not exceed
+ *     NV4_W4A16_STATIC_SCRATCH_FLOATS; larger requests return
+ *     NV4_ERR_UNSUPPORTED before anything is launched.  m > 16 needs no scratch.
+ *   - Zero start: the split-K kernel adds into the first m * n floats of the
+ *     array, so each call clears them on `stream` (cudaMemsetAsync) first.
+ *   - Set-up: the first call on a device looks up the array's address with
+ *     that device current (cudaGetSymbolAddress, which loads the library's
+ *     kernels) and keeps it; make that first call before any stream capture.
+ *   - Concurrency: every call on one device shares the one array.  Calls that
+ *     may overlap (other streams, other host threads, without ordering between
+ *     them) race on it and give wrong results; serialise them.
+ */
+#define NV4_W4A16_STATIC_SCRATCH_FLOATS (512 * 1024)
+int nv4_w4a16_gemm_static(const void* x, const void* qweight, const void* qzeros, const void* scales, void* out,
+                          int64_t m, int64_t n, int64_t k, int64_t group_size, void* stream);
+
 /* Library metadata and error reporting. */
 int nv4_version(void);                      /* major*10000 + minor*100 + patch */
 const char* nv4_status_string(int status);  /* static string for a status code */

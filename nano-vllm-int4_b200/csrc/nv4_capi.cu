@@ -254,5 +254,22 @@ int nv4_w4a16_gemm(const void* x, const void* qweight, const void* qzeros, const
                            static_cast<cudaStream_t>(stream));
 }
 
+// Allocation-free variant: the split-K partials go to a static device array
+// (see launch_w4a16_gemm_static).  Checks as nv4_w4a16_gemm, plus the
+// scratch limit.
+int nv4_w4a16_gemm_static(const void* x, const void* qweight, const void* qzeros, const void* scales, void* out,
+                          int64_t m, int64_t n, int64_t k, int64_t group_size, void* stream) {
+  if (!x || !qweight || !qzeros || !scales || !out) return NV4_ERR_INVALID_ARGUMENT;
+  if (group_size != 128) return NV4_ERR_UNSUPPORTED;
+  if (m < 1 || n < 64 || k < 128 || k % 128 || n % 64 || m > (int64_t(1) << 31) - 1 || k > (int64_t(1) << 24) ||
+      n > (int64_t(1) << 24))
+    return NV4_ERR_INVALID_ARGUMENT;
+  if (!w4a16_static_fits(m, n)) return NV4_ERR_UNSUPPORTED;
+  if (!aligned(x, 16) || !aligned(qweight, 4) || !aligned(qzeros, 4) || !aligned(scales, 2) || !aligned(out, 4))
+    return NV4_ERR_ALIGNMENT;
+  if (!device_is_sm100()) return NV4_ERR_DEVICE;
+  return launch_w4a16_gemm_static(x, qweight, qzeros, scales, out, m, n, k, static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"
 #pragma GCC visibility pop

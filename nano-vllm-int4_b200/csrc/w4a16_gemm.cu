@@ -211,3 +211,62 @@ int launch_w4a16_gemm(const void* x, const void* qweight, const void* qzeros, co
 }
 
 }  // namespace nv4
+
+// ---- Allocation-free variant (nv4_w4a16_gemm_static) -----------------------
+// The split-K partials go to this fixed array instead of a caller workspace.
+// Static device memory is set up when the library's module loads, so a call
+// that uses it allocates nothing.  One array per device; calls that overlap in
+// time on one device race on it (documented at the C entry point).
+#include <atomic>
+#include <mutex>
+
+namespace nv4 {
+
+constexpr int64_t kW4A16StaticScratchFloats = NV4_W4A16_STATIC_SCRATCH_FLOATS;
+constexpr int64_t kW4A16SplitMaxM = 16;  // plan_w4a16: split-K only for m <= 16
+
+static __device__ __align__(256) float g_w4a16_static_scratch[kW4A16StaticScratchFloats];
+
+// Device address of the scratch array on the current device, looked up once
+// per device (with that device current) and cached.
+static int w4a16_static_scratch(float** ptr) {
+  constexpr int kDevices = 64;
+  static std::atomic<float*> cache[kDevices];
+  static std::mutex mu;
+  const int dev = current_device();
+  if (dev < 0 || dev >= kDevices) return NV4_ERR_CUDA;
+  float* p = cache[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    std::lock_guard<std::mutex> lock(mu);
+    p = cache[dev].load(std::memory_order_relaxed);
+    if (p == nullptr) {
+      void* addr = nullptr;
+      const cudaError_t e = cudaGetSymbolAddress(&addr, g_w4a16_static_scratch);
+      if (e != cudaSuccess) {
+        set_last_cuda_error(e);
+        return NV4_ERR_CUDA;
+      }
+      p = static_cast<float*>(addr);
+      cache[dev].store(p, std::memory_order_release);
+    }
+  }
+  *ptr = p;
+  return NV4_OK;
+}
+
+// True when (m, n) fits the scratch: m > 16 never splits K, m <= 16 may.
+bool w4a16_static_fits(int64_t m, int64_t n) {
+  return m > kW4A16SplitMaxM || m * n <= kW4A16StaticScratchFloats;
+}
+
+int launch_w4a16_gemm_static(const void* x, const void* qweight, const void* qzeros, const void* scales, void* out,
+                             int64_t m, int64_t n, int64_t k, cudaStream_t stream) {
+  float* scratch = nullptr;
+  const int rc = w4a16_static_scratch(&scratch);
+  if (rc != NV4_OK) return rc;
+  // The shared launcher zeroes the first m * n floats before the split-K pass.
+  return launch_w4a16_gemm(x, qweight, qzeros, scales, out, m, n, k, scratch,
+                           kW4A16StaticScratchFloats * static_cast<int64_t>(sizeof(float)), stream);
+}
+
+}  // namespace nv4

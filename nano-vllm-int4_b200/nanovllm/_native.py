@@ -34,7 +34,7 @@ GEMM_FORCE_STREAM = 4
 
 EXPORTS = ("nv4_rht_quant_pack", "nv4_rht_quant_i8", "nv4_w4a4_grouped_gemm", "nv4_w4a4_gemm_i8", "nv4_w4a4_group_dots", "nv4_w4a16_gemm",
            "nv4_w4a16_workspace_bytes", "nv4_version", "nv4_status_string", "nv4_last_cuda_error",
-           "nv4_device_error")
+           "nv4_device_error", "nv4_w4a16_gemm_static")
 
 
 class NativeLibraryError(RuntimeError):
@@ -97,6 +97,8 @@ def load(path: str | None = None) -> ctypes.CDLL:
         lib.nv4_w4a4_gemm_i8.argtypes = [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]
         lib.nv4_w4a4_group_dots.argtypes = [_vp, _vp, _vp, _i64, _i64, _i64, _vp]
         lib.nv4_w4a16_gemm.argtypes = [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _vp]
+        lib.nv4_w4a16_gemm_static.argtypes = [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]
+        lib.nv4_w4a16_gemm_static.restype = _int
         lib.nv4_w4a16_workspace_bytes.argtypes = [_i64, _i64, _i64]
         lib.nv4_w4a16_workspace_bytes.restype = _i64
         lib.nv4_status_string.argtypes = [_int]
@@ -185,3 +187,22 @@ def w4a16_gemm(x, qweight, qzeros, scales, out, group_size: int, workspace) -> N
     with torch.cuda.device(x.device):
         check(load().nv4_w4a16_gemm(ptr(x), ptr(qweight), ptr(qzeros), ptr(scales), ptr(out), m, n, k, group_size,
                                     ws_ptr, ws_bytes, stream_of(x)), "nv4_w4a16_gemm")
+
+
+W4A16_STATIC_SCRATCH_FLOATS = 512 * 1024  # NV4_W4A16_STATIC_SCRATCH_FLOATS
+
+
+def w4a16_gemm_static(x, qweight, qzeros, scales, out, group_size: int) -> None:
+    """nv4_w4a16_gemm without a workspace: split-K partials go to the library's
+    static per-device array, so the call allocates nothing.  Overlapping calls
+    on one device race on that array; for m <= 16, m * n is limited to
+    W4A16_STATIC_SCRATCH_FLOATS (ValueError beyond it)."""
+    m, k = x.shape
+    n = qweight.shape[1]
+    with torch.cuda.device(x.device):
+        status = load().nv4_w4a16_gemm_static(ptr(x), ptr(qweight), ptr(qzeros), ptr(scales), ptr(out), m, n, k,
+                                              group_size, stream_of(x))
+        if status == ERR_UNSUPPORTED and group_size == 128 and m <= 16 and m * n > W4A16_STATIC_SCRATCH_FLOATS:
+            raise ValueError(f"nv4_w4a16_gemm_static: m * n = {m * n} exceeds the static scratch of "
+                             f"{W4A16_STATIC_SCRATCH_FLOATS} floats (m <= 16); use nv4_w4a16_gemm with a workspace")
+        check(status, "nv4_w4a16_gemm_static")
