@@ -430,7 +430,10 @@ int launch_rht_quant(const void* x, const void* signs, void* packed, void* codes
     warps = std::max<int64_t>(a.ncb, (warps / a.ncb) * a.ncb);
     a.warps_used = static_cast<int>(warps);
     const int blocks = static_cast<int>((warps + 7) / 8);
-    return launch_kernel(rht_block128_kernel, dim3(blocks), dim3(256), 0, stream, false, a);
+    // Programmatic dependent launch: the kernels read only the sign vector before
+    // griddepcontrol.wait and write nothing before it, so they may start while
+    // the kernel before them in the stream drains.
+    return launch_kernel(rht_block128_kernel, dim3(blocks), dim3(256), 0, stream, true, a);
   }
   RowDHArgs a;
   a.x = static_cast<const uint16_t*>(x);
@@ -442,7 +445,7 @@ int launch_rht_quant(const void* x, const void* signs, void* packed, void* codes
   a.clamp_lo = clamp_lo;
   if (k == 4096) {
     const int blocks = static_cast<int>(std::min<int64_t>(m, static_cast<int64_t>(sms) * 8));
-    return launch_kernel(rht_rowdh4096_kernel, dim3(blocks), dim3(128), 0, stream, false, a);
+    return launch_kernel(rht_rowdh4096_kernel, dim3(blocks), dim3(128), 0, stream, true, a);
   }
   static bool attr_set[64] = {};
   const int dev = current_device();
@@ -453,7 +456,7 @@ int launch_rht_quant(const void* x, const void* signs, void* packed, void* codes
     attr_set[dev] = true;
   }
   const int blocks = static_cast<int>(std::min<int64_t>(m, static_cast<int64_t>(sms) * 4));
-  return launch_kernel(rht_rowdh12288_kernel, dim3(blocks), dim3(128), kRowDH12288Smem, stream, false, a);
+  return launch_kernel(rht_rowdh12288_kernel, dim3(blocks), dim3(128), kRowDH12288Smem, stream, true, a);
 }
 
 }  // namespace nv4

@@ -132,14 +132,16 @@ def test_extreme_scales(cuda_device):
     np.testing.assert_array_equal(got32.numpy(), oracle_out(qa, qw, sa, sw))
 
 
-@pytest.mark.parametrize("force_stream", [False, True], ids=["tcgen05", "mma_sync"])
+@pytest.mark.parametrize("path", ["default", "mma_sync", "tc_decode"])
 @pytest.mark.parametrize("grouped", [True, False])
 @pytest.mark.parametrize("m,n,k", [(1, 6144, 4096), (8, 4096, 4096), (32, 24576, 4096), (32, 4096, 12288),
                                    (17, 96, 512), (33, 136, 4096), (100, 64, 2048), (5, 24, 384),
-                                   (128, 256, 4096), (300, 512, 1024), (1024, 384, 12288)])
-def test_i8_activation_gemm_exact(cuda_device, m, n, k, grouped, force_stream):
-    """nv4_w4a4_gemm_i8 (the path W4A4Linear uses) equals the oracle bit for bit,
-    on the tcgen05 kernel and on the mma.sync kernel."""
+                                   (128, 256, 4096), (300, 512, 1024), (1024, 384, 12288),
+                                   (16, 30720, 1024), (3, 38016, 256), (24, 1000, 640)])
+def test_i8_activation_gemm_exact(cuda_device, m, n, k, grouped, path):
+    """nv4_w4a4_gemm_i8 (the path W4A4Linear uses) equals the oracle bit for bit
+    on every kernel: the default dispatch (tcgen05 above 64 tokens, mma.sync
+    below), the mma.sync kernel forced, and the tcgen05 decode kernel."""
     from gpu_helpers import codes_to_i8_layout
     g = torch.Generator().manual_seed(m * 7 + n + k)
     qa = torch.randint(-8, 8, (m, k), generator=g, dtype=torch.int8)
@@ -151,7 +153,7 @@ def test_i8_activation_gemm_exact(cuda_device, m, n, k, grouped, force_stream):
     for fp32 in (False, True):
         out = Guarded((m, n), torch.float32 if fp32 else torch.bfloat16, d, -1234.0, float("nan"))
         wk.w4a4_grouped_gemm_i8(a8, pack(qw).to(d), sa.to(d), sw.to(d), out=out.view, out_fp32=fp32,
-                                force_stream=force_stream)
+                                force_stream=path == "mma_sync", tc_decode=path == "tc_decode")
         torch.cuda.synchronize()
         assert out.intact()
         ref = oracle_out(qa, qw, sa, sw)
@@ -162,7 +164,8 @@ def test_i8_activation_gemm_exact(cuda_device, m, n, k, grouped, force_stream):
     assert _native.device_error() == 0
 
 
-def test_i8_gemm_extreme_scales_use_exact_path(cuda_device):
+@pytest.mark.parametrize("tc_decode", [False, True], ids=["mma_sync", "tc_decode"])
+def test_i8_gemm_extreme_scales_use_exact_path(cuda_device, tc_decode):
     """Scales outside the two-FMA fast range take the reference's three-step form."""
     from gpu_helpers import codes_to_i8_layout
     m, n, k = 16, 64, 1024
@@ -176,5 +179,5 @@ def test_i8_gemm_extreme_scales_use_exact_path(cuda_device):
     sw[3, 2] = 2.0 ** -120
     d = cuda_device
     got = wk.w4a4_grouped_gemm_i8(codes_to_i8_layout(qa).to(d), pack(qw).to(d), sa.to(d), sw.to(d),
-                                  out_fp32=True).cpu().numpy()
+                                  out_fp32=True, tc_decode=tc_decode).cpu().numpy()
     np.testing.assert_array_equal(got, oracle_out(qa, qw, sa, sw))
