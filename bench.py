@@ -72,6 +72,20 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
+TRAFFIC_PROFILE = os.path.join(ROOT, "profiles", "w4a4_stream_gemm_m32.md")
+
+
+def profiled_traffic():
+    """DRAM bytes (read + write) of one gate/up GEMM launch from the committed
+    ncu capture of this kernel, or None when the summary is absent."""
+    import re
+    if not os.path.exists(TRAFFIC_PROFILE):
+        return None
+    with open(TRAFFIC_PROFILE) as f:
+        m = re.search(r"gate/up traffic per launch \(dram read \+ write\): (\d+) bytes", f.read())
+    return int(m.group(1)) if m else None
+
+
 # ---------------------------------------------------------------- clocks (NVML, read-only)
 class ClockSampler(threading.Thread):
     REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
@@ -331,6 +345,7 @@ def main():
     achieved = gemm_b / t_gemm / 1e9
 
     total_bytes = step_bytes(M_TOKENS, args.layers)
+    weight_bytes = args.layers * sum(n * k // 2 + 2 * n * k // 128 for _, n, k in SHAPES)
     value = total_bytes * args.steps / dt / 1e9
     e2e = total_bytes * args.steps / dt_e2e / 1e9
     launches = 2 * 4 * args.layers * args.steps
@@ -342,7 +357,8 @@ def main():
             "data": "synthetic (random-init weights, N(0,1) activations)",
             "config": {"workload": "config1-decode-chain", "m_tokens": M_TOKENS, "layers": args.layers,
                        "shapes": {n: [nn, kk] for n, nn, kk in SHAPES}, "layout": "block128", "clamp_lo": -8,
-                       "parallelism": f"tp{world}", "l2": "weights 3.58 GB per step > 126 MB L2, no flush",
+                       "parallelism": f"tp{world}",
+                       "l2": f"weights {weight_bytes / 1e9:.2f} GB per step vs 126 MB L2, no flush",
                        "bytes_per_step": total_bytes},
             "tok_s_linears": M_TOKENS * args.steps / dt,
             "e2e": {"value": e2e, "unit": "GB/s", "h2d_bytes_per_step": x_host.numel() * 2,
@@ -352,7 +368,9 @@ def main():
             "roofline": {"bound": "hbm", "kernel": f"w4a4 grouped GEMM gate_up M=32 N={n_gu} K=4096",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": peak_kind, "bytes_per_launch": gemm_b, "us_per_launch": t_gemm * 1e6,
-                         "traffic": None},
+                         "traffic": profiled_traffic(),
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, "
+                                           "profiles/w4a4_stream_gemm_m32.md"},
             "clocks": clocks,
         }
         if world == 1 and not args.no_cpu_baseline:
