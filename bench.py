@@ -7,7 +7,8 @@ down (12288 -> 4096) -- each one activation-prep launch (block128 RHT +
 per-group INT4 quantisation + packing, codes in [-8, 7]) and one grouped INT4
 GEMM launch, with distinct random weights per layer (3.58 GB, larger than L2,
 so no flush is needed).  The next projection reads the previous one's output
-(its first K columns), as a decoder layer's linears do.  The step is captured
+(its first M*K elements viewed as [M, K], so no copy kernel sits between
+the projections), as a decoder layer's linears do.  The step is captured
 in a CUDA graph and replayed, as the reference's model runner does for decode.
 
 With ``--gpus N`` (torchrun, one rank per GPU) the layers are tensor-parallel:
@@ -161,14 +162,22 @@ def build_layers(device, layers, tp_rank, tp_size):
     return mods
 
 
+def head_view(t, k):
+    """The first M*K elements of a contiguous [M, N >= K] output as a contiguous
+    [M, K] input: keeps the data dependency between projections without a copy
+    kernel (a column slice would need one, outside the quantized-linear path)."""
+    m = t.shape[0]
+    return t.reshape(-1)[: m * k].view(m, k)
+
+
 def forward(mods, x):
     """Chained decode forward through the linears; x: [32, 4096] BF16 (replicated)."""
     h = x
     for layer in mods:
         qkv = layer["qkv"](h)
-        o = layer["o"](qkv[:, :layer["o"].in_features].contiguous())
+        o = layer["o"](head_view(qkv, layer["o"].in_features))
         gu = layer["gate_up"](o)
-        h = layer["down"](gu[:, :layer["down"].in_features].contiguous())
+        h = layer["down"](head_view(gu, layer["down"].in_features))
     return h
 
 
@@ -190,7 +199,7 @@ def cpu_layer_sample(seed=0):
     def run():
         h = xb
         for (n, k, packed, sbits, signs, codes) in weights:
-            inp = h[:, :k] if h.shape[1] >= k else h
+            inp = h.reshape(-1)[: h.shape[0] * k].reshape(h.shape[0], k)
             h = o.w4a4_linear(np.ascontiguousarray(inp), signs, packed, sbits, o.LAYOUT_BLOCK128, -8,
                               w_codes=codes)
         return h

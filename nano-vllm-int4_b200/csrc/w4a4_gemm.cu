@@ -24,6 +24,16 @@
 // prep kernel writes: INT8 codes with the same even/odd K order, so ldmatrix
 // yields MMA fragments directly) or packed (widened in registers).
 //
+// K split (narrow layers): a warp walks its stages in order, so a CTA with few
+// slabs is bound by one warp's per-stage latency times the number of stages.
+// With KS > 1 the KS warps of a slab take every KS-th stage, write the exact
+// per-group partials (dot*sa, or the dot itself off the fast path) to a
+// shared-memory block of 2*KS groups, meet at a named barrier, and then each
+// applies the FMA chain, in group order, to its 1/KS of the slab's outputs:
+// the chain and its roundings are unchanged, only the dot products run in
+// parallel.  Wide layers (many slabs per CTA) keep KS = 1 with the chain in
+// the warp that computed the dots.
+//
 // Epilogue per group: the INT32 accumulator starts at the bit pattern of
 // 1.5*2^23 and reads as the float 12582912 + 16*dot.  When both scales are in
 // a range where sa*sw is exact in FP32 (always, for the quantizer's scales),
@@ -70,8 +80,8 @@ __device__ __forceinline__ bool scale_in_fast_range(float s, float lo, float hi)
 
 // Shared-memory carve-up (byte offsets from the 1024-aligned base).
 struct StreamLayout {
-  int w_bytes, a_bytes, stage_bytes, sw_off, sa_off, sac_off, flags_off, bar_off, total;
-  __host__ __device__ StreamLayout(int R, int MP, int G, int S, bool wg) {
+  int w_bytes, a_bytes, stage_bytes, sw_off, sa_off, sac_off, flags_off, ds_off, bar_off, total;
+  __host__ __device__ StreamLayout(int R, int MP, int G, int S, bool wg, int ds_bytes) {
     w_bytes = R * 128;
     a_bytes = MP * 128;  // per group (A8) or per stage (packed)
     stage_bytes = w_bytes + 2 * a_bytes;
@@ -80,14 +90,22 @@ struct StreamLayout {
     sa_off = (sw_off + sw_bytes + 1023) & ~1023;
     sac_off = (sa_off + MP * G * 2 + 15) & ~15;
     flags_off = sac_off + MP * G * 8;
-    bar_off = (flags_off + 2 * G * 4 + 7) & ~7;
+    ds_off = (flags_off + 2 * G * 4 + 15) & ~15;  // K-split partials (KS > 1)
+    bar_off = (ds_off + ds_bytes + 7) & ~7;
     total = bar_off + (2 * S + 2) * 8 + 16;
   }
 };
 
-// MT: token tiles of 8 per CTA; TPW: token tiles per consumer warp;
-// A8: activations in the widened layout; WG: grouped weight scales; F32: FP32 out.
-template <int MT, int TPW, bool A8, bool WG, bool F32>
+// Bytes of the K-split partial blocks: per (slab, token share), two buffers of
+// 2*KS groups x 16 rows x 8*TPW tokens of FP32.
+__host__ __device__ constexpr int stream_ds_bytes(int groups_of_warps, int ks, int tpw) {
+  return ks > 1 ? groups_of_warps * 2 * (2 * ks) * (tpw * 128) * 4 : 0;
+}
+
+// MT: token tiles of 8 per CTA; TPW: token tiles per consumer warp; KS: warps
+// splitting K per slab and token share; A8: activations in the widened layout;
+// WG: grouped weight scales; F32: FP32 out.
+template <int MT, int TPW, int KS, bool A8, bool WG, bool F32>
 __global__ void __launch_bounds__(32 * (1 + kMaxConsumerWarps), 1)
     w4a4_stream_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
                        const __grid_constant__ CUtensorMap tmap_sw, const __grid_constant__ CUtensorMap tmap_sa,
@@ -95,11 +113,12 @@ __global__ void __launch_bounds__(32 * (1 + kMaxConsumerWarps), 1)
   constexpr int MP = MT * 8;
   constexpr int TS = MT / TPW;        // token splits per slab
   constexpr int GI = TPW >= 4 ? 1 : 2;  // groups whose MMAs are interleaved
+  constexpr int E = TPW * 4 / KS;       // chain elements per lane and warp (K split)
   extern __shared__ uint8_t smem_raw[];
   const int S = p.stages, R = p.R, G = p.G;
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  const StreamLayout L(R, MP, G, S, WG);
+  const StreamLayout L(R, MP, G, S, WG, stream_ds_bytes(p.slabs * TS, KS, TPW));
   uint16_t* sw_s = reinterpret_cast<uint16_t*>(smem + L.sw_off);   // [R][G] (or [R])
   uint16_t* sa_s = reinterpret_cast<uint16_t*>(smem + L.sa_off);   // [MP][G]
   float2* sac = reinterpret_cast<float2*>(smem + L.sac_off);       // [G][MP]: (sa/16, -786432*sa)
@@ -110,14 +129,14 @@ __global__ void __launch_bounds__(32 * (1 + kMaxConsumerWarps), 1)
   int* issued = reinterpret_cast<int*>(scale_bar + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int consumer_warps = p.slabs * TS;
+  const int consumer_warps = p.slabs * TS * KS;
   const int n0 = blockIdx.x * R, m0 = blockIdx.y * MP;
   const uint32_t a_tile_bytes = A8 ? 2u * L.a_bytes : static_cast<uint32_t>(L.a_bytes);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], consumer_warps);
+      mbar_init(&empty[s], consumer_warps / KS);  // one warp per (slab, token share) reads a stage
     }
     mbar_init(&scale_bar[0], 1);
     mbar_init(&scale_bar[1], 1);
@@ -186,7 +205,8 @@ __global__ void __launch_bounds__(32 * (1 + kMaxConsumerWarps), 1)
   const int cw = warp - 1;
   const int ct = threadIdx.x - 32, cthreads = 32 * consumer_warps;
   const bool active = cw < consumer_warps;
-  const int slab = cw / TS, tile0 = (cw % TS) * TPW;
+  const int grp = cw / KS, ks = cw % KS;  // (slab, token share) group; K-split index within it
+  const int slab = grp / TS, tile0 = (grp % TS) * TPW;
   const int gid = lane >> 2, tig = lane & 3;
 
   // Scales: by TMA when the rows are 16-byte multiples, else cooperative loads.
@@ -229,175 +249,286 @@ __global__ void __launch_bounds__(32 * (1 + kMaxConsumerWarps), 1)
   named_barrier_sync(1, cthreads);
   if (!active) return;
 
-  float tot[TPW][4];
-#pragma unroll
-  for (int t = 0; t < TPW; ++t)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) tot[t][i] = 0.0f;
-
   const uint32_t sbase = smem_u32(smem);
   const int row_lo = slab * 16 + gid, row_hi = row_lo + 8;
-  int it = 0;
-  for (; ok && it < p.n_iters; ++it) {
-    const int slot = it % S;
-    if (!mbar_wait(&full[slot], (it / S) & 1, kErrTimeoutFull)) {
-      ok = false;
-      break;
-    }
-    const uint32_t wbase = sbase + slot * L.stage_bytes, abase = wbase + L.w_bytes;
-    // GI groups are processed together so that GI * TPW independent MMA chains
-    // are in flight; all fragment loads of a batch are issued before its MMAs.
+  const uint32_t lrow = slab * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+  // acc reads as F = 12582912 + S*dot, S = 16 (A8: codes x 16-weights) or 256
+  constexpr float kInvS = A8 ? 0.0625f : 0.00390625f;
+  constexpr float kOff = A8 ? -786432.0f : -49152.0f;
+
+  // Bias-seeded INT32 accumulators of groups gb .. gb+GI-1 of the stage at
+  // (wbase, abase), for this warp's slab and token tiles.  GI groups are
+  // processed together so that GI * TPW independent MMA chains are in flight;
+  // all fragment loads of a batch are issued before its MMAs.
+  auto stage_mma = [&](uint32_t wbase, uint32_t abase, int gb, int (&acc)[GI][TPW][4]) {
+    uint32_t aw[GI][4][4];    // widened weight fragments [group][k32 step][a0..a3]
+    uint32_t bq[GI][TPW][8];  // token fragments [group][tile][k32 step x (b0, b1)]
 #pragma unroll
-    for (int gb = 0; gb < 2; gb += GI) {
-      uint32_t aw[GI][4][4];       // widened weight fragments [group][k32 step][a0..a3]
-      uint32_t bq[GI][TPW][8];     // token fragments [group][tile][k32 step x (b0, b1)]
-      const uint32_t lrow = slab * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+    for (int gi = 0; gi < GI; ++gi) {
+      const int gg = gb + gi;
+      uint32_t af[2][4];
+      ldmatrix_x4(wbase + sw128_offset(lrow, gg * 4 + (lane >> 4)), af[0][0], af[0][1], af[0][2], af[0][3]);
+      ldmatrix_x4(wbase + sw128_offset(lrow, gg * 4 + 2 + (lane >> 4)), af[1][0], af[1][1], af[1][2], af[1][3]);
 #pragma unroll
-      for (int gi = 0; gi < GI; ++gi) {
-        const int gg = gb + gi;
-        uint32_t af[2][4];
-        ldmatrix_x4(wbase + sw128_offset(lrow, gg * 4 + (lane >> 4)), af[0][0], af[0][1], af[0][2], af[0][3]);
-        ldmatrix_x4(wbase + sw128_offset(lrow, gg * 4 + 2 + (lane >> 4)), af[1][0], af[1][1], af[1][2], af[1][3]);
+      for (int t = 0; t < TPW; ++t) {
+        const uint32_t trow = (tile0 + t) * 8 + (lane & 7);
+        if (A8) {
+          const uint32_t ab = abase + gg * L.a_bytes;
+          ldmatrix_x4(ab + sw128_offset(trow, lane >> 3), bq[gi][t][0], bq[gi][t][1], bq[gi][t][2], bq[gi][t][3]);
+          ldmatrix_x4(ab + sw128_offset(trow, 4 + (lane >> 3)), bq[gi][t][4], bq[gi][t][5], bq[gi][t][6],
+                      bq[gi][t][7]);
+        } else {
+          uint32_t bf[4];
+          ldmatrix_x4(abase + sw128_offset(trow, gg * 4 + (lane >> 3)), bf[0], bf[1], bf[2], bf[3]);
 #pragma unroll
-        for (int t = 0; t < TPW; ++t) {
-          const uint32_t trow = (tile0 + t) * 8 + (lane & 7);
-          if (A8) {
-            const uint32_t ab = abase + gg * L.a_bytes;
-            ldmatrix_x4(ab + sw128_offset(trow, lane >> 3), bq[gi][t][0], bq[gi][t][1], bq[gi][t][2], bq[gi][t][3]);
-            ldmatrix_x4(ab + sw128_offset(trow, 4 + (lane >> 3)), bq[gi][t][4], bq[gi][t][5], bq[gi][t][6],
-                        bq[gi][t][7]);
-          } else {
-            uint32_t bf[4];
-            ldmatrix_x4(abase + sw128_offset(trow, gg * 4 + (lane >> 3)), bf[0], bf[1], bf[2], bf[3]);
-#pragma unroll
-            for (int w = 0; w < 4; ++w) {
-              bq[gi][t][2 * w] = nib_even16(bf[w]);
-              bq[gi][t][2 * w + 1] = nib_odd16(bf[w]);
-            }
+          for (int w = 0; w < 4; ++w) {
+            bq[gi][t][2 * w] = nib_even16(bf[w]);
+            bq[gi][t][2 * w + 1] = nib_odd16(bf[w]);
           }
         }
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          aw[gi][2 * h][0] = nib_even16(af[h][0]);
-          aw[gi][2 * h][1] = nib_even16(af[h][1]);
-          aw[gi][2 * h][2] = nib_odd16(af[h][0]);
-          aw[gi][2 * h][3] = nib_odd16(af[h][1]);
-          aw[gi][2 * h + 1][0] = nib_even16(af[h][2]);
-          aw[gi][2 * h + 1][1] = nib_even16(af[h][3]);
-          aw[gi][2 * h + 1][2] = nib_odd16(af[h][2]);
-          aw[gi][2 * h + 1][3] = nib_odd16(af[h][3]);
-        }
       }
-      int acc[GI][TPW][4];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        aw[gi][2 * h][0] = nib_even16(af[h][0]);
+        aw[gi][2 * h][1] = nib_even16(af[h][1]);
+        aw[gi][2 * h][2] = nib_odd16(af[h][0]);
+        aw[gi][2 * h][3] = nib_odd16(af[h][1]);
+        aw[gi][2 * h + 1][0] = nib_even16(af[h][2]);
+        aw[gi][2 * h + 1][1] = nib_even16(af[h][3]);
+        aw[gi][2 * h + 1][2] = nib_odd16(af[h][2]);
+        aw[gi][2 * h + 1][3] = nib_odd16(af[h][3]);
+      }
+    }
+#pragma unroll
+    for (int gi = 0; gi < GI; ++gi)
+#pragma unroll
+      for (int t = 0; t < TPW; ++t)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[gi][t][i] = kMagicBits;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
 #pragma unroll
       for (int gi = 0; gi < GI; ++gi)
 #pragma unroll
         for (int t = 0; t < TPW; ++t)
+          mma_s8_16832(acc[gi][t], aw[gi][q][0], aw[gi][q][1], aw[gi][q][2], aw[gi][q][3], bq[gi][t][2 * q],
+                       bq[gi][t][2 * q + 1]);
+  };
+
+  auto store_out = [&](int row, int tok, float v) {
+    const int rr = n0 + row, tk = m0 + tok;
+    if (tk < p.M && rr < p.N) {
+      if (!WG) v = __fmul_rn(v, bf16_bits_to_f32(sw_s[row]));
+      const size_t o = static_cast<size_t>(tk) * p.N + rr;
+      if (F32)
+        static_cast<float*>(p.out)[o] = v;
+      else
+        static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(v);
+    }
+  };
+
+  if constexpr (KS == 1) {
+    float tot[TPW][4];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) acc[gi][t][i] = kMagicBits;
+    for (int t = 0; t < TPW; ++t)
 #pragma unroll
-      for (int q = 0; q < 4; ++q)
+      for (int i = 0; i < 4; ++i) tot[t][i] = 0.0f;
+    int it = 0;
+    for (; ok && it < p.n_iters; ++it) {
+      const int slot = it % S;
+      if (!mbar_wait(&full[slot], (it / S) & 1, kErrTimeoutFull)) {
+        ok = false;
+        break;
+      }
+      const uint32_t wbase = sbase + slot * L.stage_bytes, abase = wbase + L.w_bytes;
 #pragma unroll
-        for (int gi = 0; gi < GI; ++gi)
+      for (int gb = 0; gb < 2; gb += GI) {
+        int acc[GI][TPW][4];
+        stage_mma(wbase, abase, gb, acc);
 #pragma unroll
-          for (int t = 0; t < TPW; ++t)
-            mma_s8_16832(acc[gi][t], aw[gi][q][0], aw[gi][q][1], aw[gi][q][2], aw[gi][q][3], bq[gi][t][2 * q],
-                         bq[gi][t][2 * q + 1]);
-      // acc reads as F = 12582912 + S*dot, S = 16 (A8: codes x 16-weights) or 256
-      constexpr float kInvS = A8 ? 0.0625f : 0.00390625f;
-      constexpr float kOff = A8 ? -786432.0f : -49152.0f;
+        for (int gi = 0; gi < GI; ++gi) {  // groups in increasing order
+          const int g = it * 2 + gb + gi;
+          if (g >= G) break;
+          float sw0 = 1.0f, sw1 = 1.0f;
+          if (WG) {
+            sw0 = bf16_bits_to_f32(sw_s[row_lo * G + g]);
+            sw1 = bf16_bits_to_f32(sw_s[row_hi * G + g]);
+          }
+          const bool fast = A8 && fast_g[g] != 0;
 #pragma unroll
-      for (int gi = 0; gi < GI; ++gi) {   // groups in increasing order
-        const int g = it * 2 + gb + gi;
-        if (g >= G) break;
-        float sw0 = 1.0f, sw1 = 1.0f;
-        if (WG) {
-          sw0 = bf16_bits_to_f32(sw_s[row_lo * G + g]);
-          sw1 = bf16_bits_to_f32(sw_s[row_hi * G + g]);
-        }
-        const bool fast = A8 && fast_g[g] != 0;
-#pragma unroll
-        for (int t = 0; t < TPW; ++t) {
-          const int* a = acc[gi][t];
-          const int tok = (tile0 + t) * 8 + tig * 2;
-          if (fast) {
-            const float4 c = *reinterpret_cast<const float4*>(&sac[g * MP + tok]);  // (sa0/16, c0, sa1/16, c1)
-            const float ds0 = fmaf(__int_as_float(a[0]), c.x, c.y);
-            const float ds1 = fmaf(__int_as_float(a[1]), c.z, c.w);
-            const float ds2 = fmaf(__int_as_float(a[2]), c.x, c.y);
-            const float ds3 = fmaf(__int_as_float(a[3]), c.z, c.w);
-            if (WG) {
-              tot[t][0] = fmaf(ds0, sw0, tot[t][0]);
-              tot[t][1] = fmaf(ds1, sw0, tot[t][1]);
-              tot[t][2] = fmaf(ds2, sw1, tot[t][2]);
-              tot[t][3] = fmaf(ds3, sw1, tot[t][3]);
+          for (int t = 0; t < TPW; ++t) {
+            const int* a = acc[gi][t];
+            const int tok = (tile0 + t) * 8 + tig * 2;
+            if (fast) {
+              const float4 c = *reinterpret_cast<const float4*>(&sac[g * MP + tok]);  // (sa0/16, c0, sa1/16, c1)
+              const float ds0 = fmaf(__int_as_float(a[0]), c.x, c.y);
+              const float ds1 = fmaf(__int_as_float(a[1]), c.z, c.w);
+              const float ds2 = fmaf(__int_as_float(a[2]), c.x, c.y);
+              const float ds3 = fmaf(__int_as_float(a[3]), c.z, c.w);
+              if (WG) {
+                tot[t][0] = fmaf(ds0, sw0, tot[t][0]);
+                tot[t][1] = fmaf(ds1, sw0, tot[t][1]);
+                tot[t][2] = fmaf(ds2, sw1, tot[t][2]);
+                tot[t][3] = fmaf(ds3, sw1, tot[t][3]);
+              } else {
+                tot[t][0] = __fadd_rn(tot[t][0], ds0);
+                tot[t][1] = __fadd_rn(tot[t][1], ds1);
+                tot[t][2] = __fadd_rn(tot[t][2], ds2);
+                tot[t][3] = __fadd_rn(tot[t][3], ds3);
+              }
             } else {
-              tot[t][0] = __fadd_rn(tot[t][0], ds0);
-              tot[t][1] = __fadd_rn(tot[t][1], ds1);
-              tot[t][2] = __fadd_rn(tot[t][2], ds2);
-              tot[t][3] = __fadd_rn(tot[t][3], ds3);
-            }
-          } else {
-            const float sa0 = bf16_bits_to_f32(sa_s[tok * G + g]);
-            const float sa1 = bf16_bits_to_f32(sa_s[(tok + 1) * G + g]);
-            const float d0 = fmaf(__int_as_float(a[0]), kInvS, kOff);
-            const float d1 = fmaf(__int_as_float(a[1]), kInvS, kOff);
-            const float d2 = fmaf(__int_as_float(a[2]), kInvS, kOff);
-            const float d3 = fmaf(__int_as_float(a[3]), kInvS, kOff);
-            if (WG) {
-              tot[t][0] = fmaf(d0, __fmul_rn(sa0, sw0), tot[t][0]);
-              tot[t][1] = fmaf(d1, __fmul_rn(sa1, sw0), tot[t][1]);
-              tot[t][2] = fmaf(d2, __fmul_rn(sa0, sw1), tot[t][2]);
-              tot[t][3] = fmaf(d3, __fmul_rn(sa1, sw1), tot[t][3]);
-            } else {
-              tot[t][0] = fmaf(d0, sa0, tot[t][0]);
-              tot[t][1] = fmaf(d1, sa1, tot[t][1]);
-              tot[t][2] = fmaf(d2, sa0, tot[t][2]);
-              tot[t][3] = fmaf(d3, sa1, tot[t][3]);
+              const float sa0 = bf16_bits_to_f32(sa_s[tok * G + g]);
+              const float sa1 = bf16_bits_to_f32(sa_s[(tok + 1) * G + g]);
+              const float d0 = fmaf(__int_as_float(a[0]), kInvS, kOff);
+              const float d1 = fmaf(__int_as_float(a[1]), kInvS, kOff);
+              const float d2 = fmaf(__int_as_float(a[2]), kInvS, kOff);
+              const float d3 = fmaf(__int_as_float(a[3]), kInvS, kOff);
+              if (WG) {
+                tot[t][0] = fmaf(d0, __fmul_rn(sa0, sw0), tot[t][0]);
+                tot[t][1] = fmaf(d1, __fmul_rn(sa1, sw0), tot[t][1]);
+                tot[t][2] = fmaf(d2, __fmul_rn(sa0, sw1), tot[t][2]);
+                tot[t][3] = fmaf(d3, __fmul_rn(sa1, sw1), tot[t][3]);
+              } else {
+                tot[t][0] = fmaf(d0, sa0, tot[t][0]);
+                tot[t][1] = fmaf(d1, sa1, tot[t][1]);
+                tot[t][2] = fmaf(d2, sa0, tot[t][2]);
+                tot[t][3] = fmaf(d3, sa1, tot[t][3]);
+              }
             }
           }
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[slot]);
-  }
 
-  if (!ok) {
-    // Let every copy this CTA issued land before the CTA's shared memory is released.
-    if (cw == 0 && lane == 0) {
-      const int iss = *reinterpret_cast<volatile int*>(issued);
-      for (int j = it; j < iss; ++j) mbar_wait_drain(&full[j % S], (j / S) & 1);
-    }
-    return;
-  }
-
-  const int r0 = n0 + row_lo, r1 = n0 + row_hi;
-  float swc0 = 1.0f, swc1 = 1.0f;
-  if (!WG) {
-    swc0 = bf16_bits_to_f32(sw_s[row_lo]);
-    swc1 = bf16_bits_to_f32(sw_s[row_hi]);
-  }
-#pragma unroll
-  for (int t = 0; t < TPW; ++t) {
-    const int t0 = m0 + (tile0 + t) * 8 + tig * 2, t1 = t0 + 1;
-    float v[4] = {tot[t][0], tot[t][1], tot[t][2], tot[t][3]};
-    if (!WG) {
-      v[0] = __fmul_rn(v[0], swc0);
-      v[1] = __fmul_rn(v[1], swc0);
-      v[2] = __fmul_rn(v[2], swc1);
-      v[3] = __fmul_rn(v[3], swc1);
-    }
-    const int rr[4] = {r0, r0, r1, r1}, tk[4] = {t0, t1, t0, t1};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      if (tk[i] < p.M && rr[i] < p.N) {
-        const size_t o = static_cast<size_t>(tk[i]) * p.N + rr[i];
-        if (F32)
-          static_cast<float*>(p.out)[o] = v[i];
-        else
-          static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(v[i]);
+    if (!ok) {
+      // Let every copy this CTA issued land before the CTA's shared memory is released.
+      if (cw == 0 && lane == 0) {
+        const int iss = *reinterpret_cast<volatile int*>(issued);
+        for (int j = it; j < iss; ++j) mbar_wait_drain(&full[j % S], (j / S) & 1);
       }
+      return;
+    }
+#pragma unroll
+    for (int t = 0; t < TPW; ++t) {
+      const int t0 = (tile0 + t) * 8 + tig * 2;
+      store_out(row_lo, t0, tot[t][0]);
+      store_out(row_lo, t0 + 1, tot[t][1]);
+      store_out(row_hi, t0, tot[t][2]);
+      store_out(row_hi, t0 + 1, tot[t][3]);
+    }
+  } else {
+    // K split.  Partials of a block of 2*KS groups (KS stages, one per warp):
+    // [2 buffers][2*KS groups][KS chunks][32 lanes][E] FP32 per (slab, token
+    // share); chunk c of a lane holds its accumulator elements e = t*4 + i in
+    // [c*E, (c+1)*E), and warp ks applies the chain to chunk ks.
+    constexpr int BUF = 2 * KS * KS * 32 * E;
+    float* dsb = reinterpret_cast<float*>(smem + L.ds_off) + grp * 2 * BUF;
+    float tot[E];
+#pragma unroll
+    for (int o = 0; o < E; ++o) tot[o] = 0.0f;
+    const int nblk = (p.n_iters + KS - 1) / KS;
+    for (int blk = 0; blk < nblk; ++blk) {
+      float* buf = dsb + (blk & 1) * BUF;
+      const int it = blk * KS + ks;
+      if (ok && it < p.n_iters) {
+        const int slot = it % S;
+        ok = mbar_wait(&full[slot], (it / S) & 1, kErrTimeoutFull);
+        if (ok) {
+          const uint32_t wbase = sbase + slot * L.stage_bytes, abase = wbase + L.w_bytes;
+#pragma unroll
+          for (int gb = 0; gb < 2; gb += GI) {
+            int acc[GI][TPW][4];
+            stage_mma(wbase, abase, gb, acc);
+#pragma unroll
+            for (int gi = 0; gi < GI; ++gi) {
+              const int gg = gb + gi, g = it * 2 + gg;
+              if (g >= G) break;
+              const bool fast = A8 && fast_g[g] != 0;
+              float v[TPW * 4];
+#pragma unroll
+              for (int t = 0; t < TPW; ++t) {
+                const int tok = (tile0 + t) * 8 + tig * 2;
+                const float4 c = *reinterpret_cast<const float4*>(&sac[g * MP + tok]);  // (sa0/16, c0, sa1/16, c1)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  const float f = __int_as_float(acc[gi][t][i]);
+                  // fast: dot*sa (exact); otherwise the exact dot
+                  v[t * 4 + i] = fast ? ((i & 1) ? fmaf(f, c.z, c.w) : fmaf(f, c.x, c.y)) : fmaf(f, kInvS, kOff);
+                }
+              }
+              float* dst = buf + ((2 * ks + gg) * KS * 32 + lane) * E;
+#pragma unroll
+              for (int c = 0; c < KS; ++c) {
+                float* d = dst + c * 32 * E;
+                if constexpr (E % 4 == 0) {
+#pragma unroll
+                  for (int o = 0; o < E; o += 4)
+                    *reinterpret_cast<float4*>(d + o) = make_float4(v[c * E + o], v[c * E + o + 1], v[c * E + o + 2],
+                                                                     v[c * E + o + 3]);
+                } else if constexpr (E == 2) {
+                  *reinterpret_cast<float2*>(d) = make_float2(v[c * E], v[c * E + 1]);
+                } else {
+                  d[0] = v[c];
+                }
+              }
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+      }
+      named_barrier_sync(2 + grp, KS * 32);
+      // the chain over the block's groups, in increasing g, for chunk ks
+      for (int gl = 0; gl < 2 * KS; ++gl) {
+        const int g = blk * 2 * KS + gl;
+        if (g >= G) break;
+        const bool fast = A8 && fast_g[g] != 0;
+        const float* src = buf + ((gl * KS + ks) * 32 + lane) * E;
+        float v[E];
+        if constexpr (E % 4 == 0) {
+#pragma unroll
+          for (int o = 0; o < E; o += 4) {
+            const float4 x = *reinterpret_cast<const float4*>(src + o);
+            v[o] = x.x;
+            v[o + 1] = x.y;
+            v[o + 2] = x.z;
+            v[o + 3] = x.w;
+          }
+        } else if constexpr (E == 2) {
+          const float2 x = *reinterpret_cast<const float2*>(src);
+          v[0] = x.x;
+          v[1] = x.y;
+        } else {
+          v[0] = src[0];
+        }
+#pragma unroll
+        for (int o = 0; o < E; ++o) {
+          const int e = ks * E + o, t = e >> 2, i = e & 3;
+          const int row = i < 2 ? row_lo : row_hi, tok = (tile0 + t) * 8 + tig * 2 + (i & 1);
+          if (WG) {
+            const float sw = bf16_bits_to_f32(sw_s[row * G + g]);
+            tot[o] = fast ? fmaf(v[o], sw, tot[o])
+                          : fmaf(v[o], __fmul_rn(bf16_bits_to_f32(sa_s[tok * G + g]), sw), tot[o]);
+          } else {
+            tot[o] = fast ? __fadd_rn(tot[o], v[o]) : fmaf(v[o], bf16_bits_to_f32(sa_s[tok * G + g]), tot[o]);
+          }
+        }
+      }
+    }
+    if (error_raised()) {
+      // Let every copy this CTA issued land before the CTA's shared memory is released.
+      if (cw == 0 && lane == 0) {
+        const int iss = *reinterpret_cast<volatile int*>(issued);
+        for (int j = max(0, iss - S); j < iss; ++j) mbar_wait_drain(&full[j % S], (j / S) & 1);
+      }
+      return;
+    }
+#pragma unroll
+    for (int o = 0; o < E; ++o) {
+      const int e = ks * E + o, t = e >> 2, i = e & 3;
+      store_out(i < 2 ? row_lo : row_hi, (tile0 + t) * 8 + tig * 2 + (i & 1), tot[o]);
     }
   }
 }
@@ -425,29 +556,29 @@ __global__ void w4a4_group_dots_kernel(const uint8_t* __restrict__ a, const uint
 }
 
 // ------------------------------------------------------------ host side
-template <int MT, int TPW, bool A8, bool WG, bool F32>
+template <int MT, int TPW, int KS, bool A8, bool WG, bool F32>
 static int launch_t(const CUtensorMap* maps, const StreamGemmArgs& a, dim3 grid, int threads, int smem,
                     cudaStream_t stream) {
   static int done[64] = {};
-  auto* kern = &w4a4_stream_kernel<MT, TPW, A8, WG, F32>;
+  auto* kern = &w4a4_stream_kernel<MT, TPW, KS, A8, WG, F32>;
   const int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem, done);
   if (rc != NV4_OK) return rc;
   return launch_kernel(kern, grid, dim3(threads), smem, stream, true, maps[0], maps[1], maps[2], maps[3], a);
 }
 
-template <int MT, int TPW>
+template <int MT, int TPW, int KS>
 static int launch_flags(const CUtensorMap* maps, const StreamGemmArgs& a, dim3 grid, int threads, int smem, bool a8,
                         bool wg, bool f32, cudaStream_t s) {
   if (a8) {
-    if (wg) return f32 ? launch_t<MT, TPW, true, true, true>(maps, a, grid, threads, smem, s)
-                       : launch_t<MT, TPW, true, true, false>(maps, a, grid, threads, smem, s);
-    return f32 ? launch_t<MT, TPW, true, false, true>(maps, a, grid, threads, smem, s)
-               : launch_t<MT, TPW, true, false, false>(maps, a, grid, threads, smem, s);
+    if (wg) return f32 ? launch_t<MT, TPW, KS, true, true, true>(maps, a, grid, threads, smem, s)
+                       : launch_t<MT, TPW, KS, true, true, false>(maps, a, grid, threads, smem, s);
+    return f32 ? launch_t<MT, TPW, KS, true, false, true>(maps, a, grid, threads, smem, s)
+               : launch_t<MT, TPW, KS, true, false, false>(maps, a, grid, threads, smem, s);
   }
-  if (wg) return f32 ? launch_t<MT, TPW, false, true, true>(maps, a, grid, threads, smem, s)
-                     : launch_t<MT, TPW, false, true, false>(maps, a, grid, threads, smem, s);
-  return f32 ? launch_t<MT, TPW, false, false, true>(maps, a, grid, threads, smem, s)
-             : launch_t<MT, TPW, false, false, false>(maps, a, grid, threads, smem, s);
+  if (wg) return f32 ? launch_t<MT, TPW, KS, false, true, true>(maps, a, grid, threads, smem, s)
+                     : launch_t<MT, TPW, KS, false, true, false>(maps, a, grid, threads, smem, s);
+  return f32 ? launch_t<MT, TPW, KS, false, false, true>(maps, a, grid, threads, smem, s)
+             : launch_t<MT, TPW, KS, false, false, false>(maps, a, grid, threads, smem, s);
 }
 
 constexpr int kSmemLimit = 227 * 1024;
@@ -476,21 +607,24 @@ int launch_w4a4_stream_gemm(const void* a_packed, const void* a8, const void* w_
   const int64_t ctas_per_mblock = std::max<int64_t>(1, sms / std::min<int64_t>(mblocks, sms));
   int slabs = static_cast<int>(std::min<int64_t>(kMaxConsumerWarps, (total_slabs + ctas_per_mblock - 1) / ctas_per_mblock));
   slabs = std::max(1, slabs);
-  // Narrow layers: split token tiles over two warps per slab (each widens the
-  // slab's weights, so no further) when there are few slabs per CTA.
+  // Narrow layers (few slabs per CTA): split K over 4 (up to 4 slabs) or 2 (up
+  // to 8) warps per slab.  Wider ones: split token tiles over two warps per
+  // slab when that still fits (each widens the slab's weights, so no further).
+  int ks = slabs <= 4 ? 4 : (slabs <= 8 ? 2 : 1);
   int ts = 1;
-  if (MT >= 2 && slabs * 2 <= kMaxConsumerWarps && slabs < 8) ts = 2;
+  if (ks == 1 && MT >= 2 && slabs * 2 <= kMaxConsumerWarps && slabs < 8) ts = 2;
   const int tpw = MT / ts;
+  const int ds_bytes = stream_ds_bytes(slabs * ts, ks, tpw);
   const int R = slabs * 16;
   const int n_iters = (G + 1) / 2;
   const bool scale_tma = (G % 8) == 0 && (reinterpret_cast<uintptr_t>(a_scale) & 15) == 0 &&
                          (reinterpret_cast<uintptr_t>(w_scale) & 15) == 0;
-  const StreamLayout one(R, MP, G, 1, wg);
+  const StreamLayout one(R, MP, G, 1, wg, ds_bytes);
   const int fixed = one.total - one.stage_bytes;
   int stages = (kSmemLimit - 1024 - fixed - 64) / (one.stage_bytes + 16);
   stages = std::min(stages, std::min(16, n_iters));
   if (stages < 1) return NV4_ERR_UNSUPPORTED;
-  const StreamLayout lay(R, MP, G, stages, wg);
+  const StreamLayout lay(R, MP, G, stages, wg, ds_bytes);
   const int smem = lay.total + 1024;
 
   CUtensorMap maps[4];
@@ -524,14 +658,20 @@ int launch_w4a4_stream_gemm(const void* a_packed, const void* a8, const void* w_
   a.stages = stages;
   a.scale_tma = scale_tma ? 1 : 0;
   const dim3 grid(static_cast<unsigned>((n + R - 1) / R), static_cast<unsigned>(mblocks));
-  const int threads = 32 * (1 + slabs * ts);
-  switch (MT * 10 + tpw) {
-    case 11: return launch_flags<1, 1>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
-    case 21: return launch_flags<2, 1>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
-    case 22: return launch_flags<2, 2>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
-    case 41: return launch_flags<4, 1>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
-    case 42: return launch_flags<4, 2>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
-    case 44: return launch_flags<4, 4>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
+  const int threads = 32 * (1 + slabs * ts * ks);
+  switch (MT * 100 + tpw * 10 + ks) {
+    case 111: return launch_flags<1, 1, 1>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
+    case 112: return launch_flags<1, 1, 2>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
+    case 114: return launch_flags<1, 1, 4>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
+    case 211: return launch_flags<2, 1, 1>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
+    case 221: return launch_flags<2, 2, 1>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
+    case 222: return launch_flags<2, 2, 2>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
+    case 224: return launch_flags<2, 2, 4>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
+    case 411: return launch_flags<4, 1, 1>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
+    case 421: return launch_flags<4, 2, 1>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
+    case 441: return launch_flags<4, 4, 1>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
+    case 442: return launch_flags<4, 4, 2>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
+    case 444: return launch_flags<4, 4, 4>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
     default: return NV4_ERR_UNSUPPORTED;
   }
 }
