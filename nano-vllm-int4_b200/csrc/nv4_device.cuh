@@ -19,6 +19,7 @@ namespace nv4 {
 // Exact float32 values (hex literals): fl32(sqrt(128)), fl32(1/sqrt(12)),
 // fl32(1/7), fl32(0.9) and the BF16 "tiny" (2^-126).
 constexpr float kSqrt128 = 0x1.6a09e6p+3f;
+constexpr float kInvSqrt128 = 0x1.6a09e6p-4f;  // RN(1 / kSqrt128)
 constexpr float kInvSqrt12 = 0x1.279a74p-2f;
 constexpr float kInv7 = 0x1.24924ap-3f;
 constexpr float kClip = 0x1.ccccccp-1f;

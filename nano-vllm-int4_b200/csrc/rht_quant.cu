@@ -17,6 +17,10 @@
 // the BF16 tiny, code = round-half-even(__fdiv_rn(x, scale)) clamped to
 // [clamp_lo, 7], two codes per byte with the even K index in the low nibble.
 //
+// The two divisions are computed without the IEEE division sequence where
+// that gives the same result (div_sqrt128 and quant_code below say why), and
+// fall back to __fdiv_rn where it might not.
+//
 // The butterflies map index bits to registers (3 low bits inside a 16-byte
 // load), to lanes (warp shuffles) and, for the full-width layout, to warps (one
 // shared-memory exchange); the FP32 result of every butterfly equals the
@@ -49,8 +53,26 @@ __device__ __forceinline__ float round_scale(float s, uint16_t* bits) {
   return __bfloat162float(b);
 }
 
-__device__ __forceinline__ int quant_code(float v, float sf, int clamp_lo) {
-  int c = __float2int_rn(__fdiv_rn(v, sf));
+// x / fl32(sqrt(128)), correctly rounded: q0 = x*r, then one Newton-style
+// correction with the exact residual fma(-q0, d, x).  For this divisor the
+// result equals the IEEE quotient for every significand once |x| >= 2^-100
+// (checked exhaustively on the host, tests/test_prep_arith_cpu.py); below that
+// the intermediates may be subnormal and the IEEE division is used.
+__device__ __forceinline__ float div_sqrt128(float x) {
+  const float q0 = x * kInvSqrt128;
+  const float q1 = fmaf(fmaf(-q0, kSqrt128, x), kInvSqrt128, q0);
+  return fabsf(x) >= 0x1p-100f ? q1 : __fdiv_rn(x, kSqrt128);
+}
+
+// round-half-even(fl32(v / sf)) clamped, with rs = RN(1/sf).  The scale makes
+// |v / sf| < 7.82, where q = RN(v * rs) is within 2^-19 of the rounded
+// quotient, so both round to the same integer unless q is within 2^-17 of a
+// half-integer; there the IEEE quotient decides.
+__device__ __forceinline__ int quant_code(float v, float sf, float rs, int clamp_lo) {
+  const float q = v * rs;
+  float k = rintf(q);
+  if (fabsf(fabsf(q - k) - 0.5f) < 0x1p-17f) k = rintf(__fdiv_rn(v, sf));
+  int c = __float2int_rn(k);
   c = max(c, clamp_lo);
   return min(c, 7);
 }
@@ -63,9 +85,10 @@ __device__ __forceinline__ int quant_code(float v, float sf, int clamp_lo) {
 //    GEMM's INT4->INT8 weight widening produces, so its MMA operands match.
 __device__ __forceinline__ void store_codes(const float (&v)[8], float sf, int clamp_lo, uint8_t* packed_row,
                                             int8_t* i8_row, int k8) {
+  const float rs = __frcp_rn(sf);
   int c[8];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) c[e] = quant_code(v[e], sf, clamp_lo);
+  for (int e = 0; e < 8; ++e) c[e] = quant_code(v[e], sf, rs, clamp_lo);
   if (packed_row != nullptr) {
     uint32_t word = 0;
 #pragma unroll
@@ -140,55 +163,55 @@ struct Block128Args {
   int M, K, G, ncb, warps_used, clamp_lo;
 };
 
-// A warp owns 8 consecutive groups (one "column block") of a row; lane q of
-// quad `quad` holds elements idx = j*32 + q*8 + e of group cb*8 + quad
-// (j: index bits 5-6, q: bits 3-4, e: bits 0-2).  Warps keep their column
-// block, and so their signs, while striding over rows.
+// A warp owns GPW = 32 / LPG consecutive groups (one "column block") of a row;
+// the LPG lanes of group slot `slot` hold elements idx = j*8*LPG + l*8 + e of
+// group cb*GPW + slot (e: index bits 0-2, l: the next log2(LPG) bits, j: the
+// rest).  Warps keep their column block, and so their signs, while striding
+// over rows.  LPG = 8 halves each lane's work for decode batches; LPG = 4
+// needs fewer shuffles for large batches.
+template <int LPG>
 __global__ void __launch_bounds__(256) rht_block128_kernel(const Block128Args p) {
+  constexpr int J = 16 / LPG;    // 8-element register blocks per lane
+  constexpr int GPW = 32 / LPG;  // groups per warp
   grid_dependents_launch();
   const int lane = threadIdx.x & 31;
-  const int gw = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (gw >= p.warps_used) return;
   const int cb = gw % p.ncb;
   const int row_step = p.warps_used / p.ncb;
-  const int quad = lane >> 2, q = lane & 3;
-  const int g = cb * 8 + quad;
+  const int slot = lane / LPG, l = lane % LPG;
+  const int g = cb * GPW + slot;
   const bool active = g < p.G;
-  const bool hi1 = (q & 1) != 0, hi2 = (q & 2) != 0;
 
-  uint32_t sb[4] = {0, 0, 0, 0};
-  if (active) {
+  uint32_t sb[J];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) sb[j] = sign_bits8(p.signs + g * 128 + j * 32 + q * 8);
-  }
+  for (int j = 0; j < J; ++j) sb[j] = active ? sign_bits8(p.signs + g * 128 + j * 8 * LPG + l * 8) : 0u;
   grid_dependency_wait();
 
   for (int row = gw / p.ncb; row < p.M; row += row_step) {
-    float v[4][8];
+    float v[J][8];
     if (active) {
-      const uint16_t* src = p.x + static_cast<size_t>(row) * p.K + g * 128 + q * 8;
+      const uint16_t* src = p.x + static_cast<size_t>(row) * p.K + g * 128 + l * 8;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) load8_signed(src + j * 32, sb[j], v[j]);
+      for (int j = 0; j < J; ++j) load8_signed(src + j * 8 * LPG, sb[j], v[j]);
     } else {
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
+      for (int j = 0; j < J; ++j)
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[j][e] = 0.0f;
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) butterfly8(v[j]);                                  // bits 0-2
+    for (int j = 0; j < J; ++j) butterfly8(v[j]);  // bits 0-2
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+    for (int m = 1; m < LPG; m <<= 1)               // the lane bits
 #pragma unroll
-      for (int e = 0; e < 8; ++e) v[j][e] = butterfly_lane(v[j][e], 1, hi1);      // bit 3
+      for (int j = 0; j < J; ++j)
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+        for (int e = 0; e < 8; ++e) v[j][e] = butterfly_lane(v[j][e], m, (l & m) != 0);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) v[j][e] = butterfly_lane(v[j][e], 2, hi2);      // bit 4
+    for (int s = 1; s < J; s <<= 1) {               // the register-block bits
 #pragma unroll
-    for (int s = 1; s < 4; s <<= 1) {                                              // bits 5-6
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
+      for (int j = 0; j < J; ++j) {
         if (!(j & s)) {
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
@@ -201,22 +224,22 @@ __global__ void __launch_bounds__(256) rht_block128_kernel(const Block128Args p)
     }
     float mx = 0.0f;
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+    for (int j = 0; j < J; ++j)
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        v[j][e] = __fdiv_rn(v[j][e], kSqrt128);
+        v[j][e] = div_sqrt128(v[j][e]);
         mx = fmaxf(mx, fabsf(v[j][e]));
       }
-    mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 1));
-    mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 2));
+#pragma unroll
+    for (int m = 1; m < LPG; m <<= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, m));
     uint16_t sbits;
     const float sf = round_scale(scale_block128(mx), &sbits);
     if (active) {
       uint8_t* prow = p.packed ? p.packed + static_cast<size_t>(row) * (p.K / 2) : nullptr;
       int8_t* irow = p.codes8 ? p.codes8 + static_cast<size_t>(row) * p.K : nullptr;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) store_codes(v[j], sf, p.clamp_lo, prow, irow, g * 128 + j * 32 + q * 8);
-      if (q == 0) p.scale[static_cast<size_t>(row) * p.G + g] = sbits;
+      for (int j = 0; j < J; ++j) store_codes(v[j], sf, p.clamp_lo, prow, irow, g * 128 + j * 8 * LPG + l * 8);
+      if (l == 0) p.scale[static_cast<size_t>(row) * p.G + g] = sbits;
     }
   }
 }
@@ -423,17 +446,23 @@ int launch_rht_quant(const void* x, const void* signs, void* packed, void* codes
     a.M = static_cast<int>(m);
     a.K = static_cast<int>(k);
     a.G = static_cast<int>(k / 128);
-    a.ncb = (a.G + 7) / 8;
     a.clamp_lo = clamp_lo;
+    // Decode-sized batches: 8 lanes per group and 4-warp CTAs, so the few rows
+    // spread over many SMs with little work per lane; large batches: 4 lanes
+    // per group, 8-warp CTAs.
+    const bool small = m <= 256;
+    const int gpw = small ? 4 : 8, wpb = small ? 4 : 8;
+    a.ncb = (a.G + gpw - 1) / gpw;
     const int64_t tasks = m * a.ncb;
     int64_t warps = std::min<int64_t>(tasks, static_cast<int64_t>(sms) * 32);
     warps = std::max<int64_t>(a.ncb, (warps / a.ncb) * a.ncb);
     a.warps_used = static_cast<int>(warps);
-    const int blocks = static_cast<int>((warps + 7) / 8);
+    const int blocks = static_cast<int>((warps + wpb - 1) / wpb);
     // Programmatic dependent launch: the kernels read only the sign vector before
     // griddepcontrol.wait and write nothing before it, so they may start while
     // the kernel before them in the stream drains.
-    return launch_kernel(rht_block128_kernel, dim3(blocks), dim3(256), 0, stream, true, a);
+    if (small) return launch_kernel(rht_block128_kernel<8>, dim3(blocks), dim3(32 * wpb), 0, stream, true, a);
+    return launch_kernel(rht_block128_kernel<4>, dim3(blocks), dim3(32 * wpb), 0, stream, true, a);
   }
   RowDHArgs a;
   a.x = static_cast<const uint16_t*>(x);
