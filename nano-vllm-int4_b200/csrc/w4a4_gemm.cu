@@ -61,6 +61,7 @@ struct StreamGemmArgs {
 };
 
 constexpr int kMaxConsumerWarps = 16;
+constexpr int kProducerWarps = 4;
 
 __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
   const uint64_t start = global_timer_ns();
@@ -106,7 +107,7 @@ __host__ __device__ constexpr int stream_ds_bytes(int groups_of_warps, int ks, i
 // splitting K per slab and token share; A8: activations in the widened layout;
 // WG: grouped weight scales; F32: FP32 out.
 template <int MT, int TPW, int KS, bool A8, bool WG, bool F32>
-__global__ void __launch_bounds__(32 * (1 + kMaxConsumerWarps), 1)
+__global__ void __launch_bounds__(32 * (kProducerWarps + kMaxConsumerWarps), 1)
     w4a4_stream_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
                        const __grid_constant__ CUtensorMap tmap_sw, const __grid_constant__ CUtensorMap tmap_sa,
                        const StreamGemmArgs p) {
@@ -126,7 +127,6 @@ __global__ void __launch_bounds__(32 * (1 + kMaxConsumerWarps), 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
   uint64_t* empty = full + S;
   uint64_t* scale_bar = empty + S;      // [0]: weight scales, [1]: activation scales
-  int* issued = reinterpret_cast<int*>(scale_bar + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int consumer_warps = p.slabs * TS * KS;
@@ -140,40 +140,37 @@ __global__ void __launch_bounds__(32 * (1 + kMaxConsumerWarps), 1)
     }
     mbar_init(&scale_bar[0], 1);
     mbar_init(&scale_bar[1], 1);
-    *issued = 0;
     fence_mbar_init();
   }
   __syncthreads();
 
-  if (warp == 0) {
-    // ---------------- producer
+  if (warp < kProducerWarps) {
+    // ---------------- producers: warp w issues stages w, w + P, ... (one
+    // thread each).  Issuing a TMA copy costs the issuing thread ~100 cycles,
+    // so one thread cannot keep a narrow layer's stages coming; the copies of
+    // several issuing warps overlap.
     if (lane == 0) {
-      tma_prefetch_desc(&tmap_w);
-      tma_prefetch_desc(&tmap_a);
+      const int pw = warp;
       const uint64_t wpol = policy_evict_first();
-      if (p.scale_tma) {
-        mbar_arrive_expect_tx(&scale_bar[0], static_cast<uint32_t>((WG ? R * G : R) * 2));
-        if (WG)
-          tma_load_2d(sw_s, &tmap_sw, &scale_bar[0], 0, n0);
-        else
-          tma_load_2d(sw_s, &tmap_sw, &scale_bar[0], n0, 0);
+      if (pw == 0) {
+        tma_prefetch_desc(&tmap_w);
+        tma_prefetch_desc(&tmap_a);
+        if (p.scale_tma) {
+          mbar_arrive_expect_tx(&scale_bar[0], static_cast<uint32_t>((WG ? R * G : R) * 2));
+          if (WG)
+            tma_load_2d(sw_s, &tmap_sw, &scale_bar[0], 0, n0);
+          else
+            tma_load_2d(sw_s, &tmap_sw, &scale_bar[0], n0, 0);
+        }
       }
       const uint32_t bytes = static_cast<uint32_t>(L.w_bytes) + a_tile_bytes;
-      const int first = min(S, p.n_iters);
-      // A CTA's TMA requests are served roughly in order, so only a couple of
-      // weight stages go out ahead of the activation scales: the consumers
-      // need those scales before their first group.
-      const int early = min(first, 2);
-      for (int s = 0; s < early; ++s) {
-        mbar_arrive_expect_tx(&full[s], bytes);
-        tma_load_2d_hint(smem + s * L.stage_bytes, &tmap_w, &full[s], s * 128, n0, wpol);
-      }
-      grid_dependency_wait();  // activations and their scales come from the preceding kernel
-      if (p.scale_tma) {
-        mbar_arrive_expect_tx(&scale_bar[1], static_cast<uint32_t>(MP * G * 2));
-        tma_load_2d(sa_s, &tmap_sa, &scale_bar[1], 0, m0);
-      }
-      auto load_a = [&](int slot, int it) {
+      auto load_w = [&](int it) {
+        const int slot = it % S;
+        mbar_arrive_expect_tx(&full[slot], bytes);
+        tma_load_2d_hint(smem + slot * L.stage_bytes, &tmap_w, &full[slot], it * 128, n0, wpol);
+      };
+      auto load_a = [&](int it) {
+        const int slot = it % S;
         uint8_t* dst = smem + slot * L.stage_bytes + L.w_bytes;
         if (A8) {
           tma_load_2d(dst, &tmap_a, &full[slot], it * 256, m0);
@@ -182,28 +179,36 @@ __global__ void __launch_bounds__(32 * (1 + kMaxConsumerWarps), 1)
           tma_load_2d(dst, &tmap_a, &full[slot], it * 128, m0);
         }
       };
-      for (int s = 0; s < early; ++s) load_a(s, s);
-      for (int s = early; s < first; ++s) {
-        mbar_arrive_expect_tx(&full[s], bytes);
-        tma_load_2d_hint(smem + s * L.stage_bytes, &tmap_w, &full[s], s * 128, n0, wpol);
-        load_a(s, s);
+      // A CTA's TMA requests are served roughly in order, so only a couple of
+      // weight stages go out ahead of the activation scales: the consumers
+      // need those scales before their first group.
+      const int early = min(min(S, p.n_iters), 2);
+      for (int it = pw; it < early; it += kProducerWarps) load_w(it);
+      grid_dependency_wait();  // activations and their scales come from the preceding kernel
+      if (pw == 0 && p.scale_tma) {
+        mbar_arrive_expect_tx(&scale_bar[1], static_cast<uint32_t>(MP * G * 2));
+        tma_load_2d(sa_s, &tmap_sa, &scale_bar[1], 0, m0);
       }
-      *reinterpret_cast<volatile int*>(issued) = first;
-      for (int it = S; it < p.n_iters; ++it) {
-        const int slot = it % S;
-        if (!mbar_wait(&empty[slot], ((it / S) - 1) & 1, kErrTimeoutEmpty)) break;
-        mbar_arrive_expect_tx(&full[slot], bytes);
-        tma_load_2d_hint(smem + slot * L.stage_bytes, &tmap_w, &full[slot], it * 128, n0, wpol);
-        load_a(slot, it);
-        *reinterpret_cast<volatile int*>(issued) = it + 1;
+      int last = -1;
+      for (int it = pw; it < p.n_iters; it += kProducerWarps) {
+        if (it >= early) {
+          if (it >= S && !mbar_wait(&empty[it % S], ((it / S) - 1) & 1, kErrTimeoutEmpty)) break;
+          load_w(it);
+        }
+        load_a(it);
+        last = it;
+      }
+      if (error_raised()) {
+        // Before the CTA may exit, the copies this thread issued must have landed.
+        for (int it = last; it >= 0 && it > last - S; it -= kProducerWarps) mbar_wait_drain(&full[it % S], (it / S) & 1);
       }
     }
     return;
   }
 
   // ---------------- consumers
-  const int cw = warp - 1;
-  const int ct = threadIdx.x - 32, cthreads = 32 * consumer_warps;
+  const int cw = warp - kProducerWarps;
+  const int ct = threadIdx.x - 32 * kProducerWarps, cthreads = 32 * consumer_warps;
   const bool active = cw < consumer_warps;
   const int grp = cw / KS, ks = cw % KS;  // (slab, token share) group; K-split index within it
   const int slab = grp / TS, tile0 = (grp % TS) * TPW;
@@ -402,14 +407,7 @@ __global__ void __launch_bounds__(32 * (1 + kMaxConsumerWarps), 1)
       if (lane == 0) mbar_arrive(&empty[slot]);
     }
 
-    if (!ok) {
-      // Let every copy this CTA issued land before the CTA's shared memory is released.
-      if (cw == 0 && lane == 0) {
-        const int iss = *reinterpret_cast<volatile int*>(issued);
-        for (int j = it; j < iss; ++j) mbar_wait_drain(&full[j % S], (j / S) & 1);
-      }
-      return;
-    }
+    if (!ok) return;  // the producers let their copies land before the CTA exits
 #pragma unroll
     for (int t = 0; t < TPW; ++t) {
       const int t0 = (tile0 + t) * 8 + tig * 2;
@@ -517,14 +515,7 @@ __global__ void __launch_bounds__(32 * (1 + kMaxConsumerWarps), 1)
         }
       }
     }
-    if (error_raised()) {
-      // Let every copy this CTA issued land before the CTA's shared memory is released.
-      if (cw == 0 && lane == 0) {
-        const int iss = *reinterpret_cast<volatile int*>(issued);
-        for (int j = max(0, iss - S); j < iss; ++j) mbar_wait_drain(&full[j % S], (j / S) & 1);
-      }
-      return;
-    }
+    if (error_raised()) return;  // the producers let their copies land before the CTA exits
 #pragma unroll
     for (int o = 0; o < E; ++o) {
       const int e = ks * E + o, t = e >> 2, i = e & 3;
@@ -658,7 +649,7 @@ int launch_w4a4_stream_gemm(const void* a_packed, const void* a8, const void* w_
   a.stages = stages;
   a.scale_tma = scale_tma ? 1 : 0;
   const dim3 grid(static_cast<unsigned>((n + R - 1) / R), static_cast<unsigned>(mblocks));
-  const int threads = 32 * (1 + slabs * ts * ks);
+  const int threads = 32 * (kProducerWarps + slabs * ts * ks);
   switch (MT * 100 + tpw * 10 + ks) {
     case 111: return launch_flags<1, 1, 1>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
     case 112: return launch_flags<1, 1, 2>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
