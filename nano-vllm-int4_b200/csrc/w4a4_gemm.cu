@@ -257,6 +257,20 @@ __global__ void __launch_bounds__(32 * (kProducerWarps + kMaxConsumerWarps), 1)
   const uint32_t sbase = smem_u32(smem);
   const int row_lo = slab * 16 + gid, row_hi = row_lo + 8;
   const uint32_t lrow = slab * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+  constexpr uint32_t kATile = MP * 128;  // bytes of one token tile per group
+  // Loop-invariant swizzled ldmatrix offsets of this lane: weights [group][half],
+  // widened tokens [tile][half] or packed tokens [group][tile].
+  uint32_t off_w[2][2], off_a[TPW][2];
+#pragma unroll
+  for (int gg = 0; gg < 2; ++gg)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) off_w[gg][h] = sw128_offset(lrow, gg * 4 + 2 * h + (lane >> 4));
+#pragma unroll
+  for (int t = 0; t < TPW; ++t) {
+    const uint32_t trow = (tile0 + t) * 8 + (lane & 7);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) off_a[t][h] = A8 ? sw128_offset(trow, 4 * h + (lane >> 3)) : sw128_offset(trow, h * 4 + (lane >> 3));
+  }
   // acc reads as F = 12582912 + S*dot, S = 16 (A8: codes x 16-weights) or 256
   constexpr float kInvS = A8 ? 0.0625f : 0.00390625f;
   constexpr float kOff = A8 ? -786432.0f : -49152.0f;
@@ -272,19 +286,17 @@ __global__ void __launch_bounds__(32 * (kProducerWarps + kMaxConsumerWarps), 1)
     for (int gi = 0; gi < GI; ++gi) {
       const int gg = gb + gi;
       uint32_t af[2][4];
-      ldmatrix_x4(wbase + sw128_offset(lrow, gg * 4 + (lane >> 4)), af[0][0], af[0][1], af[0][2], af[0][3]);
-      ldmatrix_x4(wbase + sw128_offset(lrow, gg * 4 + 2 + (lane >> 4)), af[1][0], af[1][1], af[1][2], af[1][3]);
+      ldmatrix_x4(wbase + off_w[gg][0], af[0][0], af[0][1], af[0][2], af[0][3]);
+      ldmatrix_x4(wbase + off_w[gg][1], af[1][0], af[1][1], af[1][2], af[1][3]);
 #pragma unroll
       for (int t = 0; t < TPW; ++t) {
-        const uint32_t trow = (tile0 + t) * 8 + (lane & 7);
         if (A8) {
-          const uint32_t ab = abase + gg * L.a_bytes;
-          ldmatrix_x4(ab + sw128_offset(trow, lane >> 3), bq[gi][t][0], bq[gi][t][1], bq[gi][t][2], bq[gi][t][3]);
-          ldmatrix_x4(ab + sw128_offset(trow, 4 + (lane >> 3)), bq[gi][t][4], bq[gi][t][5], bq[gi][t][6],
-                      bq[gi][t][7]);
+          const uint32_t ab = abase + gg * kATile;
+          ldmatrix_x4(ab + off_a[t][0], bq[gi][t][0], bq[gi][t][1], bq[gi][t][2], bq[gi][t][3]);
+          ldmatrix_x4(ab + off_a[t][1], bq[gi][t][4], bq[gi][t][5], bq[gi][t][6], bq[gi][t][7]);
         } else {
           uint32_t bf[4];
-          ldmatrix_x4(abase + sw128_offset(trow, gg * 4 + (lane >> 3)), bf[0], bf[1], bf[2], bf[3]);
+          ldmatrix_x4(abase + off_a[t][gg], bf[0], bf[1], bf[2], bf[3]);
 #pragma unroll
           for (int w = 0; w < 4; ++w) {
             bq[gi][t][2 * w] = nib_even16(bf[w]);
@@ -599,10 +611,12 @@ int launch_w4a4_stream_gemm(const void* a_packed, const void* a8, const void* w_
   int slabs = static_cast<int>(std::min<int64_t>(kMaxConsumerWarps, (total_slabs + ctas_per_mblock - 1) / ctas_per_mblock));
   slabs = std::max(1, slabs);
   // Narrow layers (few slabs per CTA): split K over 4 (up to 4 slabs) or 2 (up
-  // to 8) warps per slab.  Wider ones: split token tiles over two warps per
-  // slab when that still fits (each widens the slab's weights, so no further).
-  int ks = slabs <= 4 ? 4 : (slabs <= 8 ? 2 : 1);
-  int ts = 1;
+  // to 8) warps per slab, and with 32 tokens and at most 2 slabs also split the
+  // token tiles over two warps (16 consumer warps).  Wider ones: split token
+  // tiles over two warps per slab when that still fits (each widens the slab's
+  // weights, so no further).
+  const int ks = slabs <= 4 ? 4 : (slabs <= 8 ? 2 : 1);
+  int ts = (ks == 4 && MT == 4 && slabs <= 2) ? 2 : 1;
   if (ks == 1 && MT >= 2 && slabs * 2 <= kMaxConsumerWarps && slabs < 8) ts = 2;
   const int tpw = MT / ts;
   const int ds_bytes = stream_ds_bytes(slabs * ts, ks, tpw);
@@ -662,6 +676,7 @@ int launch_w4a4_stream_gemm(const void* a_packed, const void* a8, const void* w_
     case 421: return launch_flags<4, 2, 1>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
     case 441: return launch_flags<4, 4, 1>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
     case 442: return launch_flags<4, 4, 2>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
+    case 424: return launch_flags<4, 2, 4>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
     case 444: return launch_flags<4, 4, 4>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
     default: return NV4_ERR_UNSUPPORTED;
   }
