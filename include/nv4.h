@@ -6,7 +6,9 @@
  *
  * Conventions for every entry point:
  *   - plain device pointers and sizes; no framework types;
- *   - all buffers are caller-owned; nothing is retained across calls;
+ *   - all buffers are caller-owned; nothing is retained across calls (the
+ *     set-up calls nv4_peer_buffer_alloc / _free / _open / _close manage the
+ *     tensor-parallel peer buffers and are the only ones that allocate);
  *   - work is enqueued on `stream` (a cudaStream_t passed as void*; NULL is the
  *     legacy default stream) with no host synchronisation, no allocation and no
  *     device-wide synchronisation, so every entry point may be captured in a
@@ -150,6 +152,40 @@ int64_t nv4_w4a16_workspace_bytes(int64_t m, int64_t n, int64_t k);
 #define NV4_W4A16_STATIC_SCRATCH_FLOATS (512 * 1024)
 int nv4_w4a16_gemm_static(const void* x, const void* qweight, const void* qzeros, const void* scales, void* out,
                           int64_t m, int64_t n, int64_t k, int64_t group_size, void* stream);
+
+/*
+ * One-shot all-reduce of the row-parallel layers over NVLink peer memory (the
+ * W4A4 counterpart of nanovllm/layers/linear.py:154-155, dist.all_reduce of
+ * the partial outputs; the reference has no W4A4 tensor parallelism).
+ *
+ * Every rank allocates one peer buffer at set-up for outputs of up to
+ * `capacity` elements: NV4_PEER_HEADER_BYTES of flags (zeroed), its FP32
+ * partial [capacity] and the inboxes for the other ranks' partials.  The CUDA
+ * IPC handles (NV4_IPC_HANDLE_BYTES each) are exchanged over the process
+ * group and opened on the other ranks; one buffer serves every row-parallel
+ * layer of the group.  Per call, the row-parallel GEMM writes its FP32 partial
+ * at bufs[rank] + NV4_PEER_HEADER_BYTES, then nv4_peer_allreduce_bf16 copies
+ * it into the peers' inboxes, waits for theirs, sums the partials in rank
+ * order (identical results on all ranks) and writes BF16 [count] to `out`.
+ * All ranks must make the same sequence of calls with the same counts; the
+ * per-call synchronisation state lives in the buffers, so the calls may be
+ * replayed from a CUDA graph.  A rank that does not arrive within 2 s makes
+ * the others record an error (see nv4_device_error) and return.
+ *
+ *   bufs      world pointers: this rank's buffer at [rank], the opened peers' others
+ *   world     2..8
+ *   count     elements of this call, a multiple of 4, <= capacity
+ *   capacity  the capacity every rank allocated with (a multiple of 4)
+ */
+#define NV4_PEER_HEADER_BYTES 4096
+#define NV4_IPC_HANDLE_BYTES 64
+int64_t nv4_peer_header_bytes(void);
+int nv4_peer_buffer_alloc(int64_t capacity, void** buf, void* ipc_handle);
+int nv4_peer_buffer_open(const void* ipc_handle, void** buf);
+int nv4_peer_buffer_close(void* buf);  /* a buffer opened with nv4_peer_buffer_open */
+int nv4_peer_buffer_free(void* buf);   /* a buffer from nv4_peer_buffer_alloc */
+int nv4_peer_allreduce_bf16(void* const* bufs, int rank, int world, void* out, int64_t count, int64_t capacity,
+                            void* stream);
 
 /* Library metadata and error reporting. */
 int nv4_version(void);                      /* major*10000 + minor*100 + patch */

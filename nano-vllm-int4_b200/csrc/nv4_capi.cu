@@ -1,6 +1,7 @@
 // C ABI of libnv4 (declared in include/nv4.h): argument checks that mirror the
 // reference's Python validation, then dispatch to the kernel launchers.
 #include <cstdint>
+#include <cstring>
 #include <mutex>
 
 #include "nv4_device.cuh"
@@ -279,6 +280,70 @@ int nv4_w4a16_gemm_static(const void* x, const void* qweight, const void* qzeros
     return NV4_ERR_ALIGNMENT;
   if (!device_is_sm100()) return NV4_ERR_DEVICE;
   return launch_w4a16_gemm_static(x, qweight, qzeros, scales, out, m, n, k, static_cast<cudaStream_t>(stream));
+}
+
+// ---- peer buffers and the one-shot all-reduce of the row-parallel layers
+int64_t nv4_peer_header_bytes(void) { return NV4_PEER_HEADER_BYTES; }
+
+int nv4_peer_buffer_alloc(int64_t capacity, void** buf, void* ipc_handle) {
+  if (!buf || !ipc_handle || capacity < 4 || capacity % 4 || capacity > (int64_t(1) << 28)) return NV4_ERR_INVALID_ARGUMENT;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, static_cast<size_t>(NV4_PEER_HEADER_BYTES + peer_buffer_data_bytes(capacity)));
+  if (e == cudaSuccess) e = cudaMemset(p, 0, static_cast<size_t>(NV4_PEER_HEADER_BYTES));
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    if (p) cudaFree(p);
+    set_last_cuda_error(e);
+    return NV4_ERR_CUDA;
+  }
+  memcpy(ipc_handle, &h, sizeof(h));
+  *buf = p;
+  return NV4_OK;
+}
+
+int nv4_peer_buffer_open(const void* ipc_handle, void** buf) {
+  if (!ipc_handle || !buf) return NV4_ERR_INVALID_ARGUMENT;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(buf, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return NV4_ERR_CUDA;
+  }
+  return NV4_OK;
+}
+
+int nv4_peer_buffer_close(void* buf) {
+  if (!buf) return NV4_ERR_INVALID_ARGUMENT;
+  const cudaError_t e = cudaIpcCloseMemHandle(buf);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return NV4_ERR_CUDA;
+  }
+  return NV4_OK;
+}
+
+int nv4_peer_buffer_free(void* buf) {
+  if (!buf) return NV4_ERR_INVALID_ARGUMENT;
+  const cudaError_t e = cudaFree(buf);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return NV4_ERR_CUDA;
+  }
+  return NV4_OK;
+}
+
+int nv4_peer_allreduce_bf16(void* const* bufs, int rank, int world, void* out, int64_t count, int64_t capacity,
+                            void* stream) {
+  if (!bufs || !out || world < 2 || world > 8 || rank < 0 || rank >= world || count < 4 || count % 4 ||
+      capacity % 4 || count > capacity)
+    return NV4_ERR_INVALID_ARGUMENT;
+  for (int r = 0; r < world; ++r)
+    if (!bufs[r] || !aligned(bufs[r], 256)) return NV4_ERR_ALIGNMENT;
+  if (!aligned(out, 8)) return NV4_ERR_ALIGNMENT;
+  if (!device_is_sm100()) return NV4_ERR_DEVICE;
+  return launch_peer_allreduce_bf16(bufs, rank, world, out, count, capacity, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -69,5 +69,9 @@ int64_t w4a16_workspace_bytes(int64_t m, int64_t n, int64_t k);
 int launch_w4a16_gemm_static(const void* x, const void* qweight, const void* qzeros, const void* scales, void* out,
                              int64_t m, int64_t n, int64_t k, cudaStream_t stream);
 bool w4a16_static_fits(int64_t m, int64_t n);  // (m, n) within the static scratch
+// One-shot peer-memory all-reduce of FP32 partials to BF16 (peer_allreduce.cu).
+int launch_peer_allreduce_bf16(void* const* bufs, int rank, int world, void* out, int64_t count, int64_t capacity,
+                               cudaStream_t stream);
+int64_t peer_buffer_data_bytes(int64_t capacity);  // partial + inboxes of one peer buffer
 
 }  // namespace nv4

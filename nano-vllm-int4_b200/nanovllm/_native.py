@@ -35,7 +35,8 @@ GEMM_TC_DECODE = 8
 
 EXPORTS = ("nv4_rht_quant_pack", "nv4_rht_quant_i8", "nv4_w4a4_grouped_gemm", "nv4_w4a4_gemm_i8", "nv4_w4a4_group_dots", "nv4_w4a16_gemm",
            "nv4_w4a16_workspace_bytes", "nv4_version", "nv4_status_string", "nv4_last_cuda_error",
-           "nv4_device_error", "nv4_w4a16_gemm_static")
+           "nv4_device_error", "nv4_w4a16_gemm_static", "nv4_peer_header_bytes", "nv4_peer_buffer_alloc",
+           "nv4_peer_buffer_open", "nv4_peer_buffer_close", "nv4_peer_buffer_free", "nv4_peer_allreduce_bf16")
 
 
 class NativeLibraryError(RuntimeError):
@@ -101,6 +102,16 @@ def load(path: str | None = None) -> ctypes.CDLL:
         lib.nv4_w4a16_gemm_static.argtypes = [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]
         lib.nv4_w4a16_gemm_static.restype = _int
         lib.nv4_w4a16_workspace_bytes.argtypes = [_i64, _i64, _i64]
+        lib.nv4_peer_header_bytes.argtypes = []
+        lib.nv4_peer_header_bytes.restype = _i64
+        lib.nv4_peer_buffer_alloc.argtypes = [_i64, ctypes.POINTER(_vp), _vp]
+        lib.nv4_peer_buffer_open.argtypes = [_vp, ctypes.POINTER(_vp)]
+        lib.nv4_peer_buffer_close.argtypes = [_vp]
+        lib.nv4_peer_buffer_free.argtypes = [_vp]
+        lib.nv4_peer_allreduce_bf16.argtypes = [ctypes.POINTER(_vp), _int, _int, _vp, _i64, _i64, _vp]
+        for name in ("nv4_peer_buffer_alloc", "nv4_peer_buffer_open", "nv4_peer_buffer_close", "nv4_peer_buffer_free",
+                     "nv4_peer_allreduce_bf16"):
+            getattr(lib, name).restype = _int
         lib.nv4_w4a16_workspace_bytes.restype = _i64
         lib.nv4_status_string.argtypes = [_int]
         lib.nv4_status_string.restype = ctypes.c_char_p
@@ -207,3 +218,52 @@ def w4a16_gemm_static(x, qweight, qzeros, scales, out, group_size: int) -> None:
             raise ValueError(f"nv4_w4a16_gemm_static: m * n = {m * n} exceeds the static scratch of "
                              f"{W4A16_STATIC_SCRATCH_FLOATS} floats (m <= 16); use nv4_w4a16_gemm with a workspace")
         check(status, "nv4_w4a16_gemm_static")
+
+
+# ---------------------------------------------------------------- tensor-parallel peer buffers
+IPC_HANDLE_BYTES = 64
+
+
+def peer_header_bytes() -> int:
+    return int(load().nv4_peer_header_bytes())
+
+
+def peer_buffer_alloc(capacity: int, device) -> tuple[int, bytes]:
+    """Allocate this rank's peer buffer for outputs of up to `capacity` elements
+    on `device`: (device address, IPC handle)."""
+    buf, handle = _vp(), ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    with torch.cuda.device(device):
+        check(load().nv4_peer_buffer_alloc(capacity, ctypes.byref(buf), handle), "nv4_peer_buffer_alloc")
+    return buf.value, handle.raw
+
+
+def peer_buffer_open(handle: bytes, device) -> int:
+    buf = _vp()
+    with torch.cuda.device(device):
+        check(load().nv4_peer_buffer_open(handle, ctypes.byref(buf)), "nv4_peer_buffer_open")
+    return buf.value
+
+
+def peer_buffer_close(addr: int, device) -> None:
+    with torch.cuda.device(device):
+        check(load().nv4_peer_buffer_close(_vp(addr)), "nv4_peer_buffer_close")
+
+
+def peer_buffer_free(addr: int, device) -> None:
+    with torch.cuda.device(device):
+        check(load().nv4_peer_buffer_free(_vp(addr)), "nv4_peer_buffer_free")
+
+
+def w4a4_gemm_i8_to(a_codes, w_packed, a_scale, w_scale, out_addr: int, flags: int) -> None:
+    """nv4_w4a4_gemm_i8 writing to a raw device address (a peer buffer's partial)."""
+    m, k, n = a_codes.shape[0], a_codes.shape[1], w_packed.shape[0]
+    with torch.cuda.device(a_codes.device):
+        check(load().nv4_w4a4_gemm_i8(ptr(a_codes), ptr(w_packed), ptr(a_scale), ptr(w_scale), _vp(out_addr),
+                                      m, n, k, flags, stream_of(a_codes)), "nv4_w4a4_gemm_i8")
+
+
+def peer_allreduce_bf16(bufs: list[int], rank: int, out, count: int, capacity: int) -> None:
+    arr = (_vp * len(bufs))(*[_vp(b) for b in bufs])
+    with torch.cuda.device(out.device):
+        check(load().nv4_peer_allreduce_bf16(arr, rank, len(bufs), ptr(out), count, capacity, stream_of(out)),
+              "nv4_peer_allreduce_bf16")
