@@ -13,8 +13,9 @@ in a CUDA graph and replayed, as the reference's model runner does for decode.
 
 With ``--gpus N`` (torchrun, one rank per GPU) the layers are tensor-parallel:
 QKV and gate/up split N across ranks, O and down split K on 128-group
-boundaries and sum FP32 partials with an NCCL all-reduce (strong scaling: the
-model and batch are fixed).
+boundaries and sum their FP32 partials with the one-shot peer-memory all-reduce
+kernel over NVLink (one more launch per row-parallel projection; strong
+scaling: the model and batch are fixed).
 
 ``--impl reference`` times the reference algorithm on the host CPU instead (the
 numpy oracle port of the reference's PyTorch path), on one layer of the same
@@ -357,7 +358,9 @@ def main():
     weight_bytes = args.layers * sum(n * k // 2 + 2 * n * k // 128 for _, n, k in SHAPES)
     value = total_bytes * args.steps / dt / 1e9
     e2e = total_bytes * args.steps / dt_e2e / 1e9
-    launches = 2 * 4 * args.layers * args.steps
+    from nanovllm.layers import linear_w4a4
+    peer_ar = world > 1 and any(linear_w4a4._PEER_STATE.values())  # buffers set up, else NCCL
+    launches = (2 * 4 + (2 if peer_ar else 0)) * args.layers * args.steps
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -367,6 +370,7 @@ def main():
             "config": {"workload": "config1-decode-chain", "m_tokens": M_TOKENS, "layers": args.layers,
                        "shapes": {n: [nn, kk] for n, nn, kk in SHAPES}, "layout": "block128", "clamp_lo": -8,
                        "parallelism": f"tp{world}",
+                       "allreduce": (None if world == 1 else "peer-memory one-shot kernel" if peer_ar else "nccl"),
                        "l2": f"weights {weight_bytes / 1e9:.2f} GB per step vs 126 MB L2, no flush",
                        "bytes_per_step": total_bytes},
             "tok_s_linears": M_TOKENS * args.steps / dt,
@@ -387,6 +391,7 @@ def main():
         print(json.dumps(line), flush=True)
     del graph, g_graph
     if world > 1:
+        linear_w4a4.release_peer_buffers()
         dist.barrier()
         dist.destroy_process_group()
 

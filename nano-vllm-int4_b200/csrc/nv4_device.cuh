@@ -186,6 +186,21 @@ __device__ __forceinline__ void mma_s8_16832(int (&d)[4], uint32_t a0, uint32_t 
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// d = a*b + c with a separate, loop-invariant C (the bias seed): the first
+// MMA of a group starts from c instead of re-seeding d with moves.
+__device__ __forceinline__ void mma_s8_16832_c(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1, const int (&c)[4]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%10, %11, %12, %13};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c[0]), "r"(c[1]), "r"(c[2]), "r"(c[3]));
+}
+
+// Two FP32 fused multiply-adds per instruction (sm_100 packed FP32); each
+// component is rounded as fmaf.
+__device__ __forceinline__ float2 ffma2(float2 x, float2 y, float2 z) { return __ffma2_rn(x, y, z); }
+
 // INT4 -> INT8 widening of a packed word (8 codes, code i in nibble i).  Each
 // code c becomes the int8 16*c, exact for c in [-8, 7]:
 //   nib_even16: bytes (16*c0, 16*c2, 16*c4, 16*c6)

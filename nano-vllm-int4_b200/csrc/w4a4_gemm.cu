@@ -57,10 +57,11 @@ struct StreamGemmArgs {
   int slabs;      // R / 16
   int n_iters;    // ceil(G / 2): two groups per stage
   int stages;
-  int scale_tma;  // 1: weight/activation scales arrive by TMA (G % 8 == 0)
+  int scale_tma;  // 1: weight scales arrive by TMA (G % 8 == 0, 16-byte aligned rows)
 };
 
 constexpr int kMaxConsumerWarps = 16;
+constexpr int kMaxWideSlabs = 12;  // one warp per slab (K not split): at most 16 warps, 128 registers each
 constexpr int kProducerWarps = 4;
 
 __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
@@ -107,10 +108,9 @@ __host__ __device__ constexpr int stream_ds_bytes(int groups_of_warps, int ks, i
 // splitting K per slab and token share; A8: activations in the widened layout;
 // WG: grouped weight scales; F32: FP32 out.
 template <int MT, int TPW, int KS, bool A8, bool WG, bool F32>
-__global__ void __launch_bounds__(32 * (kProducerWarps + kMaxConsumerWarps), 1)
+__global__ void __launch_bounds__(32 * (kProducerWarps + (KS == 1 && TPW == MT ? kMaxWideSlabs : kMaxConsumerWarps)), 1)
     w4a4_stream_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
-                       const __grid_constant__ CUtensorMap tmap_sw, const __grid_constant__ CUtensorMap tmap_sa,
-                       const StreamGemmArgs p) {
+                       const __grid_constant__ CUtensorMap tmap_sw, const StreamGemmArgs p) {
   constexpr int MP = MT * 8;
   constexpr int TS = MT / TPW;        // token splits per slab
   constexpr int GI = TPW >= 4 ? 1 : 2;  // groups whose MMAs are interleaved
@@ -122,24 +122,28 @@ __global__ void __launch_bounds__(32 * (kProducerWarps + kMaxConsumerWarps), 1)
   const StreamLayout L(R, MP, G, S, WG, stream_ds_bytes(p.slabs * TS, KS, TPW));
   uint16_t* sw_s = reinterpret_cast<uint16_t*>(smem + L.sw_off);   // [R][G] (or [R])
   uint16_t* sa_s = reinterpret_cast<uint16_t*>(smem + L.sa_off);   // [MP][G]
-  float2* sac = reinterpret_cast<float2*>(smem + L.sac_off);       // [G][MP]: (sa/16, -786432*sa)
-  int* fast_g = reinterpret_cast<int*>(smem + L.flags_off);        // [G]: both scales in range
+  // [G][MP/2] float4 per token pair (t, t+1): (sa_t/16, sa_t+1/16, -786432*sa_t, -786432*sa_t+1)
+  float* sac = reinterpret_cast<float*>(smem + L.sac_off);
+  int* fast_g = reinterpret_cast<int*>(smem + L.flags_off);        // [G]: both scales in range; [G]: some group not
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
   uint64_t* empty = full + S;
-  uint64_t* scale_bar = empty + S;      // [0]: weight scales, [1]: activation scales
+  uint64_t* scale_bar = empty + S;      // weight scales
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int consumer_warps = p.slabs * TS * KS;
   const int n0 = blockIdx.x * R, m0 = blockIdx.y * MP;
   const uint32_t a_tile_bytes = A8 ? 2u * L.a_bytes : static_cast<uint32_t>(L.a_bytes);
 
+  // The next kernel (activation prep, all-reduce) may launch now: its small
+  // CTAs fit beside this one and then wait in griddepcontrol.wait, which still
+  // returns only after this whole grid has completed and its writes are visible.
+  grid_dependents_launch();
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], consumer_warps / KS);  // one warp per (slab, token share) reads a stage
     }
     mbar_init(&scale_bar[0], 1);
-    mbar_init(&scale_bar[1], 1);
     fence_mbar_init();
   }
   __syncthreads();
@@ -179,16 +183,13 @@ __global__ void __launch_bounds__(32 * (kProducerWarps + kMaxConsumerWarps), 1)
           tma_load_2d(dst, &tmap_a, &full[slot], it * 128, m0);
         }
       };
-      // A CTA's TMA requests are served roughly in order, so only a couple of
-      // weight stages go out ahead of the activation scales: the consumers
-      // need those scales before their first group.
-      const int early = min(min(S, p.n_iters), 2);
+      // Every ring slot's weight tile goes out before griddepcontrol.wait: it
+      // streams while the preceding kernel finishes (the activation scales
+      // come by plain loads, so nothing the consumers need first queues
+      // behind these copies).
+      const int early = min(S, p.n_iters);
       for (int it = pw; it < early; it += kProducerWarps) load_w(it);
-      grid_dependency_wait();  // activations and their scales come from the preceding kernel
-      if (pw == 0 && p.scale_tma) {
-        mbar_arrive_expect_tx(&scale_bar[1], static_cast<uint32_t>(MP * G * 2));
-        tma_load_2d(sa_s, &tmap_sa, &scale_bar[1], 0, m0);
-      }
+      grid_dependency_wait();  // the activations come from the preceding kernel
       int last = -1;
       for (int it = pw; it < p.n_iters; it += kProducerWarps) {
         if (it >= early) {
@@ -214,8 +215,13 @@ __global__ void __launch_bounds__(32 * (kProducerWarps + kMaxConsumerWarps), 1)
   const int slab = grp / TS, tile0 = (grp % TS) * TPW;
   const int gid = lane >> 2, tig = lane & 3;
 
-  // Scales: by TMA when the rows are 16-byte multiples, else cooperative loads.
-  // No early return before the named barriers: every consumer reaches them.
+  // Weight scales (by TMA when the rows are 16-byte multiples, else cooperative
+  // loads) and their range check do not depend on the preceding kernel, so they
+  // run before griddepcontrol.wait.  The activation scales (a few KB) are then
+  // read with plain loads straight into the per-token epilogue constants.  A
+  // group leaves the two-FMA path if any of its scales is out of range (every
+  // thread checks a slice; clearing is idempotent).  No early return before the
+  // named barriers: every consumer reaches them.
   bool ok = true;
   if (!p.scale_tma) {
     if (active) {
@@ -228,31 +234,43 @@ __global__ void __launch_bounds__(32 * (kProducerWarps + kMaxConsumerWarps), 1)
   } else {
     ok = mbar_wait(&scale_bar[0], 0, kErrTimeoutFull);
   }
-  for (int g = ct; g < G; g += cthreads) fast_g[g] = 1;
-  grid_dependency_wait();
-  if (!p.scale_tma) {
-    if (active)
-      for (int i = ct; i < MP * G; i += cthreads)
-        sa_s[i] = (m0 + i / G < p.M) ? p.a_scale[static_cast<size_t>(m0) * G + i] : uint16_t(0);
-  } else {
-    ok = mbar_wait(&scale_bar[1], 0, kErrTimeoutFull) && ok;
-  }
+  for (int g = ct; g <= G; g += cthreads) fast_g[g] = g < G ? 1 : 0;
   named_barrier_sync(1, cthreads);
-  // Per-token epilogue constants; a group leaves the two-FMA path if any of its
-  // scales is out of range (every thread checks a slice; clearing is idempotent).
+  if (WG && active)
+    for (int i = ct; i < R * G; i += cthreads)
+      if (!scale_in_fast_range(bf16_bits_to_f32(sw_s[i]), 0x1.0p-30f, 0x1.0p+27f)) fast_g[i % G] = 0, fast_g[G] = 1;
+  grid_dependency_wait();
   if (active) {
-    for (int i = ct; i < MP * G; i += cthreads) {
-      const int t = i / G, g = i - t * G;
-      const float sa = bf16_bits_to_f32(sa_s[i]);
-      sac[g * MP + t] = make_float2(__fmul_rn(sa, 0.0625f), __fmul_rn(sa, -786432.0f));
-      if (!scale_in_fast_range(sa, 0x1.0p-100f, 0x1.0p+100f)) fast_g[g] = 0;
+    // eight independent loads per thread in flight: one L2 round trip for the
+    // whole [MP x G] block at decode sizes
+    constexpr int kBatch = 8;
+    const int nsa = MP * G;
+    for (int i0 = ct; i0 < nsa; i0 += kBatch * cthreads) {
+      uint16_t bits[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int i = i0 + u * cthreads;
+        bits[u] = (i < nsa && m0 + i / G < p.M) ? p.a_scale[static_cast<size_t>(m0) * G + i] : uint16_t(0);
+      }
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int i = i0 + u * cthreads;
+        if (i >= nsa) break;
+        const int t = i / G, g = i - t * G;
+        sa_s[i] = bits[u];
+        const float sa = bf16_bits_to_f32(bits[u]);
+        float* q = sac + (g * MP + (t & ~1)) * 2 + (t & 1);
+        q[0] = __fmul_rn(sa, 0.0625f);
+        q[2] = __fmul_rn(sa, -786432.0f);
+        if (!scale_in_fast_range(sa, 0x1.0p-100f, 0x1.0p+100f)) fast_g[g] = 0, fast_g[G] = 1;
+      }
     }
-    if (WG)
-      for (int i = ct; i < R * G; i += cthreads)
-        if (!scale_in_fast_range(bf16_bits_to_f32(sw_s[i]), 0x1.0p-30f, 0x1.0p+27f)) fast_g[i % G] = 0;
   }
   named_barrier_sync(1, cthreads);
   if (!active) return;
+  // Every group on the two-FMA path (the quantizer's scales always are): the
+  // epilogues take their loads out of the per-group branches.
+  const bool all_fast = A8 && fast_g[G] == 0;
 
   const uint32_t sbase = smem_u32(smem);
   const int row_lo = slab * 16 + gid, row_hi = row_lo + 8;
@@ -274,6 +292,7 @@ __global__ void __launch_bounds__(32 * (kProducerWarps + kMaxConsumerWarps), 1)
   // acc reads as F = 12582912 + S*dot, S = 16 (A8: codes x 16-weights) or 256
   constexpr float kInvS = A8 ? 0.0625f : 0.00390625f;
   constexpr float kOff = A8 ? -786432.0f : -49152.0f;
+  const int bias[4] = {kMagicBits, kMagicBits, kMagicBits, kMagicBits};  // MMA C of a group's first step
 
   // Bias-seeded INT32 accumulators of groups gb .. gb+GI-1 of the stage at
   // (wbase, abase), for this warp's slab and token tiles.  GI groups are
@@ -317,19 +336,18 @@ __global__ void __launch_bounds__(32 * (kProducerWarps + kMaxConsumerWarps), 1)
       }
     }
 #pragma unroll
-    for (int gi = 0; gi < GI; ++gi)
-#pragma unroll
-      for (int t = 0; t < TPW; ++t)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) acc[gi][t][i] = kMagicBits;
-#pragma unroll
     for (int q = 0; q < 4; ++q)
 #pragma unroll
       for (int gi = 0; gi < GI; ++gi)
 #pragma unroll
-        for (int t = 0; t < TPW; ++t)
-          mma_s8_16832(acc[gi][t], aw[gi][q][0], aw[gi][q][1], aw[gi][q][2], aw[gi][q][3], bq[gi][t][2 * q],
-                       bq[gi][t][2 * q + 1]);
+        for (int t = 0; t < TPW; ++t) {
+          if (q == 0)
+            mma_s8_16832_c(acc[gi][t], aw[gi][q][0], aw[gi][q][1], aw[gi][q][2], aw[gi][q][3], bq[gi][t][0],
+                           bq[gi][t][1], bias);
+          else
+            mma_s8_16832(acc[gi][t], aw[gi][q][0], aw[gi][q][1], aw[gi][q][2], aw[gi][q][3], bq[gi][t][2 * q],
+                         bq[gi][t][2 * q + 1]);
+        }
   };
 
   auto store_out = [&](int row, int tok, float v) {
@@ -371,28 +389,26 @@ __global__ void __launch_bounds__(32 * (kProducerWarps + kMaxConsumerWarps), 1)
             sw0 = bf16_bits_to_f32(sw_s[row_lo * G + g]);
             sw1 = bf16_bits_to_f32(sw_s[row_hi * G + g]);
           }
-          const bool fast = A8 && fast_g[g] != 0;
+          const bool fast = all_fast || (A8 && fast_g[g] != 0);
 #pragma unroll
           for (int t = 0; t < TPW; ++t) {
             const int* a = acc[gi][t];
             const int tok = (tile0 + t) * 8 + tig * 2;
             if (fast) {
-              const float4 c = *reinterpret_cast<const float4*>(&sac[g * MP + tok]);  // (sa0/16, c0, sa1/16, c1)
-              const float ds0 = fmaf(__int_as_float(a[0]), c.x, c.y);
-              const float ds1 = fmaf(__int_as_float(a[1]), c.z, c.w);
-              const float ds2 = fmaf(__int_as_float(a[2]), c.x, c.y);
-              const float ds3 = fmaf(__int_as_float(a[3]), c.z, c.w);
-              if (WG) {
-                tot[t][0] = fmaf(ds0, sw0, tot[t][0]);
-                tot[t][1] = fmaf(ds1, sw0, tot[t][1]);
-                tot[t][2] = fmaf(ds2, sw1, tot[t][2]);
-                tot[t][3] = fmaf(ds3, sw1, tot[t][3]);
-              } else {
-                tot[t][0] = __fadd_rn(tot[t][0], ds0);
-                tot[t][1] = __fadd_rn(tot[t][1], ds1);
-                tot[t][2] = __fadd_rn(tot[t][2], ds2);
-                tot[t][3] = __fadd_rn(tot[t][3], ds3);
-              }
+              // (sa0/16, sa1/16, c0, c1); ds = dot*sa, then total = fma(ds, sw, total),
+              // two elements per packed FMA
+              const float4 c = *reinterpret_cast<const float4*>(&sac[(g * MP + tok) * 2]);
+              const float2 s01 = make_float2(c.x, c.y), c01 = make_float2(c.z, c.w);
+              const float2 ds01 = ffma2(make_float2(__int_as_float(a[0]), __int_as_float(a[1])), s01, c01);
+              const float2 ds23 = ffma2(make_float2(__int_as_float(a[2]), __int_as_float(a[3])), s01, c01);
+              const float2 w0 = WG ? make_float2(sw0, sw0) : make_float2(1.0f, 1.0f);  // fma(x, 1, y) = x + y
+              const float2 w1 = WG ? make_float2(sw1, sw1) : make_float2(1.0f, 1.0f);
+              const float2 t01 = ffma2(ds01, w0, make_float2(tot[t][0], tot[t][1]));
+              const float2 t23 = ffma2(ds23, w1, make_float2(tot[t][2], tot[t][3]));
+              tot[t][0] = t01.x;
+              tot[t][1] = t01.y;
+              tot[t][2] = t23.x;
+              tot[t][3] = t23.y;
             } else {
               const float sa0 = bf16_bits_to_f32(sa_s[tok * G + g]);
               const float sa1 = bf16_bits_to_f32(sa_s[(tok + 1) * G + g]);
@@ -455,17 +471,21 @@ __global__ void __launch_bounds__(32 * (kProducerWarps + kMaxConsumerWarps), 1)
             for (int gi = 0; gi < GI; ++gi) {
               const int gg = gb + gi, g = it * 2 + gg;
               if (g >= G) break;
-              const bool fast = A8 && fast_g[g] != 0;
+              const bool fast = all_fast || (A8 && fast_g[g] != 0);
               float v[TPW * 4];
 #pragma unroll
               for (int t = 0; t < TPW; ++t) {
                 const int tok = (tile0 + t) * 8 + tig * 2;
-                const float4 c = *reinterpret_cast<const float4*>(&sac[g * MP + tok]);  // (sa0/16, c0, sa1/16, c1)
+                // fast: dot*sa (exact), with (sa0/16, sa1/16, c0, c1); otherwise the exact dot
+                const float4 c = *reinterpret_cast<const float4*>(&sac[(g * MP + tok) * 2]);
+                const float2 s01 = fast ? make_float2(c.x, c.y) : make_float2(kInvS, kInvS);
+                const float2 c01 = fast ? make_float2(c.z, c.w) : make_float2(kOff, kOff);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                  const float f = __int_as_float(acc[gi][t][i]);
-                  // fast: dot*sa (exact); otherwise the exact dot
-                  v[t * 4 + i] = fast ? ((i & 1) ? fmaf(f, c.z, c.w) : fmaf(f, c.x, c.y)) : fmaf(f, kInvS, kOff);
+                for (int h = 0; h < 2; ++h) {
+                  const float2 d = ffma2(make_float2(__int_as_float(acc[gi][t][2 * h]), __int_as_float(acc[gi][t][2 * h + 1])),
+                                         s01, c01);
+                  v[t * 4 + 2 * h] = d.x;
+                  v[t * 4 + 2 * h + 1] = d.y;
                 }
               }
               float* dst = buf + ((2 * ks + gg) * KS * 32 + lane) * E;
@@ -491,6 +511,60 @@ __global__ void __launch_bounds__(32 * (kProducerWarps + kMaxConsumerWarps), 1)
       }
       named_barrier_sync(2 + grp, KS * 32);
       // the chain over the block's groups, in increasing g, for chunk ks
+      const int gbase = blk * 2 * KS;
+      if (all_fast) {
+        // every load of the block first (partials, and the weight scales of the
+        // at most two rows this lane's elements lie in), then the FMA chain
+        float v[2 * KS][E];
+        float swv[2][2 * KS];
+#pragma unroll
+        for (int gl = 0; gl < 2 * KS; ++gl) {
+          const int g = gbase + gl;
+          const float* src = buf + ((gl * KS + ks) * 32 + lane) * E;
+          if (g < G) {
+            if constexpr (E % 4 == 0) {
+#pragma unroll
+              for (int o = 0; o < E; o += 4) {
+                const float4 x = *reinterpret_cast<const float4*>(src + o);
+                v[gl][o] = x.x;
+                v[gl][o + 1] = x.y;
+                v[gl][o + 2] = x.z;
+                v[gl][o + 3] = x.w;
+              }
+            } else if constexpr (E == 2) {
+              const float2 x = *reinterpret_cast<const float2*>(src);
+              v[gl][0] = x.x;
+              v[gl][1] = x.y;
+            } else {
+              v[gl][0] = src[0];
+            }
+          } else {
+#pragma unroll
+            for (int o = 0; o < E; ++o) v[gl][o] = 0.0f;
+          }
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+            swv[h][gl] = (WG && g < G) ? bf16_bits_to_f32(sw_s[(h ? row_hi : row_lo) * G + g]) : 1.0f;
+        }
+#pragma unroll
+        for (int gl = 0; gl < 2 * KS; ++gl) {
+          if (gbase + gl >= G) break;
+          if constexpr (E % 2 == 0) {
+#pragma unroll
+            for (int o = 0; o < E; o += 2) {
+              const float sw = ((ks * E + o) & 3) < 2 ? swv[0][gl] : swv[1][gl];  // 1 without WG: fma(x, 1, y) = x + y
+              const float2 r = ffma2(make_float2(v[gl][o], v[gl][o + 1]), make_float2(sw, sw),
+                                     make_float2(tot[o], tot[o + 1]));
+              tot[o] = r.x;
+              tot[o + 1] = r.y;
+            }
+          } else {
+#pragma unroll
+            for (int o = 0; o < E; ++o) tot[o] = fmaf(v[gl][o], ((ks * E + o) & 3) < 2 ? swv[0][gl] : swv[1][gl], tot[o]);
+          }
+        }
+        continue;
+      }
       for (int gl = 0; gl < 2 * KS; ++gl) {
         const int g = blk * 2 * KS + gl;
         if (g >= G) break;
@@ -512,6 +586,18 @@ __global__ void __launch_bounds__(32 * (kProducerWarps + kMaxConsumerWarps), 1)
           v[1] = x.y;
         } else {
           v[0] = src[0];
+        }
+        if (fast && E % 2 == 0) {
+          // elements (o, o+1) are tokens (t, t+1) of one row: one packed FMA
+#pragma unroll
+          for (int o = 0; o < E; o += 2) {
+            const int e = ks * E + o, i = e & 3;
+            const float sw = WG ? bf16_bits_to_f32(sw_s[(i < 2 ? row_lo : row_hi) * G + g]) : 1.0f;
+            const float2 r = ffma2(make_float2(v[o], v[o + 1]), make_float2(sw, sw), make_float2(tot[o], tot[o + 1]));
+            tot[o] = r.x;
+            tot[o + 1] = r.y;
+          }
+          continue;
         }
 #pragma unroll
         for (int o = 0; o < E; ++o) {
@@ -566,7 +652,7 @@ static int launch_t(const CUtensorMap* maps, const StreamGemmArgs& a, dim3 grid,
   auto* kern = &w4a4_stream_kernel<MT, TPW, KS, A8, WG, F32>;
   const int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem, done);
   if (rc != NV4_OK) return rc;
-  return launch_kernel(kern, grid, dim3(threads), smem, stream, true, maps[0], maps[1], maps[2], maps[3], a);
+  return launch_kernel(kern, grid, dim3(threads), smem, stream, true, maps[0], maps[1], maps[2], a);
 }
 
 template <int MT, int TPW, int KS>
@@ -616,14 +702,14 @@ int launch_w4a4_stream_gemm(const void* a_packed, const void* a8, const void* w_
   // tiles over two warps per slab when that still fits (each widens the slab's
   // weights, so no further).
   const int ks = slabs <= 4 ? 4 : (slabs <= 8 ? 2 : 1);
+  if (ks == 1) slabs = std::min(slabs, kMaxWideSlabs);  // wider layers take more CTAs
   int ts = (ks == 4 && MT == 4 && slabs <= 2) ? 2 : 1;
   if (ks == 1 && MT >= 2 && slabs * 2 <= kMaxConsumerWarps && slabs < 8) ts = 2;
   const int tpw = MT / ts;
   const int ds_bytes = stream_ds_bytes(slabs * ts, ks, tpw);
   const int R = slabs * 16;
   const int n_iters = (G + 1) / 2;
-  const bool scale_tma = (G % 8) == 0 && (reinterpret_cast<uintptr_t>(a_scale) & 15) == 0 &&
-                         (reinterpret_cast<uintptr_t>(w_scale) & 15) == 0;
+  const bool scale_tma = (G % 8) == 0 && (reinterpret_cast<uintptr_t>(w_scale) & 15) == 0;
   const StreamLayout one(R, MP, G, 1, wg, ds_bytes);
   const int fixed = one.total - one.stage_bytes;
   int stages = (kSmemLimit - 1024 - fixed - 64) / (one.stage_bytes + 16);
@@ -632,7 +718,7 @@ int launch_w4a4_stream_gemm(const void* a_packed, const void* a8, const void* w_
   const StreamLayout lay(R, MP, G, stages, wg, ds_bytes);
   const int smem = lay.total + 1024;
 
-  CUtensorMap maps[4];
+  CUtensorMap maps[3];
   memset(maps, 0, sizeof(maps));
   bool okm = make_tensor_map_u8(&maps[0], w_packed, n, k / 2, static_cast<uint32_t>(R), 128,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
@@ -646,7 +732,6 @@ int launch_w4a4_stream_gemm(const void* a_packed, const void* a8, const void* w_
       okm = okm && make_map_u16(&maps[2], w_scale, n, G, static_cast<uint32_t>(R), G);
     else
       okm = okm && make_map_u16(&maps[2], w_scale, 1, n, 1, static_cast<uint32_t>(R));
-    okm = okm && make_map_u16(&maps[3], a_scale, m, G, static_cast<uint32_t>(MP), G);
   }
   if (!okm) return NV4_ERR_CUDA;
 
