@@ -73,6 +73,19 @@ int nv4_rht_quant_i8(const void* x, const void* signs, void* out_codes, void* ou
                      int layout, int clamp_lo, void* stream);
 
 /*
+ * nv4_rht_quant_i8 of the down projection's input fused with its producer, the
+ * MLP's SiluAndMul (nanovllm/layers/activation.py:8-11, nanovllm/models/qwen3.py
+ * Qwen3MLP.forward): the source is the gate/up projection's output
+ *   gate_up   bf16 [m, 2k] (gate in columns 0..k-1, up in k..2k-1), 16-byte aligned
+ * and the prep input is h = bf16(silu(gate) * up), computed in FP32 with one
+ * rounding at the end as the reference's compiled SiluAndMul does
+ * (silu(g) = g / (1 + expf(-g)), IEEE division).  Outputs as nv4_rht_quant_i8
+ * for the [m, k] input h, which is never written to memory.
+ */
+int nv4_silu_mul_rht_quant_i8(const void* gate_up, const void* signs, void* out_codes, void* out_scale, int64_t m,
+                              int64_t k, int layout, int clamp_lo, void* stream);
+
+/*
  * Grouped INT4 GEMM: out[m, n] = sum_g fp32-FMA(dot_g(a, w), sa[m,g] * sw[n,g]),
  * groups of 128 along K in increasing g, one FP32 rounding per group, then BF16.
  * Replaces nanovllm/kernels/w4a4_grouped_kernel.py:104-129 (w4a4_grouped_gemm)
@@ -177,8 +190,9 @@ int nv4_w4a16_gemm_static(const void* x, const void* qweight, const void* qzeros
  *   count     elements of this call, a multiple of 4, <= capacity
  *   capacity  the capacity every rank allocated with (a multiple of 4)
  */
-#define NV4_PEER_HEADER_BYTES 4096
+#define NV4_PEER_HEADER_BYTES 16384
 #define NV4_IPC_HANDLE_BYTES 64
+#define NV4_PEER_MAX_TOKENS 32
 int64_t nv4_peer_header_bytes(void);
 int nv4_peer_buffer_alloc(int64_t capacity, void** buf, void* ipc_handle);
 int nv4_peer_buffer_open(const void* ipc_handle, void** buf);
@@ -186,6 +200,20 @@ int nv4_peer_buffer_close(void* buf);  /* a buffer opened with nv4_peer_buffer_o
 int nv4_peer_buffer_free(void* buf);   /* a buffer from nv4_peer_buffer_alloc */
 int nv4_peer_allreduce_bf16(void* const* bufs, int rank, int world, void* out, int64_t count, int64_t capacity,
                             void* stream);
+/*
+ * The row-parallel W4A4 GEMM and its all-reduce in two launches without the
+ * FP32 partial round trip: the GEMM (GEMM-ready INT8 activation codes as in
+ * nv4_w4a4_gemm_i8, up to NV4_PEER_MAX_TOKENS rows) stores each CTA's FP32
+ * output tile straight into every rank's inbox over NVLink and releases one
+ * flag per CTA on each peer; a second kernel waits for the peers' tiles and
+ * sums them in rank order to BF16 [m, n] in `out` -- the same values as
+ * nv4_w4a4_gemm_i8 (FP32) followed by nv4_peer_allreduce_bf16.  m * n must not
+ * exceed `capacity`; flags: NV4_GEMM_W_SCALE_GROUPED only.  The two forms may
+ * share one set of peer buffers; every rank makes the same sequence of calls.
+ */
+int nv4_w4a4_gemm_peer_allreduce_bf16(const void* a_codes, const void* w_packed, const void* a_scale,
+                                      const void* w_scale, void* out, int64_t m, int64_t n, int64_t k, int flags,
+                                      void* const* bufs, int rank, int world, int64_t capacity, void* stream);
 
 /* Library metadata and error reporting. */
 int nv4_version(void);                      /* major*10000 + minor*100 + patch */

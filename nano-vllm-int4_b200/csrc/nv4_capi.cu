@@ -101,10 +101,6 @@ bool make_tensor_map_u8(CUtensorMap* map, const void* base, uint64_t rows, uint6
                             swizzle);
 }
 
-int launch_w4a4_stream_gemm(const void* a_packed, const void* a8, const void* w_packed, const void* a_scale,
-                            const void* w_scale, void* out, int64_t m, int64_t n, int64_t k, int flags,
-                            cudaStream_t stream);
-
 int launch_w4a4_tc_gemm(const void* a8, const void* w_packed, const void* a_scale, const void* w_scale, void* out,
                         int64_t m, int64_t n, int64_t k, int flags, cudaStream_t stream);
 
@@ -203,6 +199,15 @@ int nv4_rht_quant_i8(const void* x, const void* signs, void* out_codes, void* ou
   if (rc != NV4_OK) return rc;
   return launch_rht_quant(x, signs, nullptr, out_codes, out_scale, m, k, layout, clamp_lo,
                           static_cast<cudaStream_t>(stream));
+}
+
+int nv4_silu_mul_rht_quant_i8(const void* gate_up, const void* signs, void* out_codes, void* out_scale, int64_t m,
+                              int64_t k, int layout, int clamp_lo, void* stream) {
+  const int rc = check_prep_args(gate_up, signs, out_codes, out_scale, m, k, layout, clamp_lo, 16);
+  if (rc != NV4_OK) return rc;
+  if (2 * k > (int64_t(1) << 24)) return NV4_ERR_INVALID_ARGUMENT;
+  return launch_silu_mul_rht_quant(gate_up, signs, nullptr, out_codes, out_scale, m, k, layout, clamp_lo,
+                                   static_cast<cudaStream_t>(stream));
 }
 
 static int check_gemm_args(const void* a, const void* w_packed, const void* a_scale, const void* w_scale,
@@ -344,6 +349,29 @@ int nv4_peer_allreduce_bf16(void* const* bufs, int rank, int world, void* out, i
   if (!aligned(out, 8)) return NV4_ERR_ALIGNMENT;
   if (!device_is_sm100()) return NV4_ERR_DEVICE;
   return launch_peer_allreduce_bf16(bufs, rank, world, out, count, capacity, static_cast<cudaStream_t>(stream));
+}
+
+int nv4_w4a4_gemm_peer_allreduce_bf16(const void* a_codes, const void* w_packed, const void* a_scale,
+                                      const void* w_scale, void* out, int64_t m, int64_t n, int64_t k, int flags,
+                                      void* const* bufs, int rank, int world, int64_t capacity, void* stream) {
+  if (flags & ~NV4_GEMM_W_SCALE_GROUPED) return NV4_ERR_INVALID_ARGUMENT;
+  const int rc = check_gemm_args(a_codes, w_packed, a_scale, w_scale, out, m, n, k, flags);
+  if (rc != NV4_OK) return rc;
+  if (!bufs || world < 2 || world > 8 || rank < 0 || rank >= world || m > NV4_PEER_MAX_TOKENS || capacity % 4 ||
+      m * n > capacity)
+    return NV4_ERR_INVALID_ARGUMENT;
+  for (int r = 0; r < world; ++r)
+    if (!bufs[r] || !aligned(bufs[r], 256)) return NV4_ERR_ALIGNMENT;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  PeerTarget peer;
+  peer.bufs = bufs;
+  peer.rank = rank;
+  peer.world = world;
+  peer.capacity = capacity;
+  const int g = launch_w4a4_stream_gemm(nullptr, a_codes, w_packed, a_scale, w_scale, nullptr, m, n, k, flags, s, &peer);
+  if (g != NV4_OK) return g;
+  return launch_peer_reduce_tiles_bf16(bufs, rank, world, out, static_cast<int>(m), static_cast<int>(n),
+                                       peer.rows_per_cta, peer.ctas, capacity, s);
 }
 
 }  // extern "C"

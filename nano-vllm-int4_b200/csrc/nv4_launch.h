@@ -57,6 +57,9 @@ bool make_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_by
 // Activation prep; `packed` and/or `codes8` (GEMM-ready INT8 layout) receive the codes.
 int launch_rht_quant(const void* x, const void* signs, void* packed, void* codes8, void* scale, int64_t m, int64_t k,
                      int layout, int clamp_lo, cudaStream_t stream);
+// Same, with the input bf16(silu(gate) * up) of a gate/up source [m, 2k].
+int launch_silu_mul_rht_quant(const void* gate_up, const void* signs, void* packed, void* codes8, void* scale,
+                              int64_t m, int64_t k, int layout, int clamp_lo, cudaStream_t stream);
 // Grouped GEMM; activations from `a8` (INT8 layout) when non-null, else `a_packed`.
 int launch_w4a4_gemm(const void* a_packed, const void* a8, const void* w_packed, const void* a_scale,
                      const void* w_scale, void* out, int64_t m, int64_t n, int64_t k, int flags, cudaStream_t stream);
@@ -69,6 +72,20 @@ int64_t w4a16_workspace_bytes(int64_t m, int64_t n, int64_t k);
 int launch_w4a16_gemm_static(const void* x, const void* qweight, const void* qzeros, const void* scales, void* out,
                              int64_t m, int64_t n, int64_t k, cudaStream_t stream);
 bool w4a16_static_fits(int64_t m, int64_t n);  // (m, n) within the static scratch
+// Peer mode of the stream GEMM (row-parallel layers): the launcher fills in the
+// tile geometry the matching tile reduce needs.
+struct PeerTarget {
+  void* const* bufs;  // world peer buffers, this rank's at [rank]
+  int rank, world;
+  int64_t capacity;
+  int rows_per_cta = 0, ctas = 0;  // out
+};
+int launch_w4a4_stream_gemm(const void* a_packed, const void* a8, const void* w_packed, const void* a_scale,
+                            const void* w_scale, void* out, int64_t m, int64_t n, int64_t k, int flags,
+                            cudaStream_t stream, PeerTarget* peer = nullptr);
+// Sum of the peer-mode GEMM's tiles in rank order to BF16 [m, n] (peer_allreduce.cu).
+int launch_peer_reduce_tiles_bf16(void* const* bufs, int rank, int world, void* out, int m, int n, int rows_per_cta,
+                                  int ctas, int64_t capacity, cudaStream_t stream);
 // One-shot peer-memory all-reduce of FP32 partials to BF16 (peer_allreduce.cu).
 int launch_peer_allreduce_bf16(void* const* bufs, int rank, int world, void* out, int64_t count, int64_t capacity,
                                cudaStream_t stream);

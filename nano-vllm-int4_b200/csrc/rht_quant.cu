@@ -120,6 +120,37 @@ __device__ __forceinline__ void load8_signed(const uint16_t* src, uint32_t sbits
   }
 }
 
+// bf16(silu(g) * u) in FP32 with one rounding at the end, as the reference's
+// compiled SiluAndMul (nanovllm/layers/activation.py:8-11: torch.compile keeps
+// the product in FP32): silu(g) = g / (1 + exp(-g)) with CUDA's expf and IEEE
+// division, as PyTorch's FP32 silu.
+__device__ __forceinline__ uint32_t silu_mul_bf16_bits(float g, float u) {
+  const float s = __fdiv_rn(g, 1.0f + expf(-g));
+  return static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(__fmul_rn(s, u))));
+}
+
+// 8 prep input values at element k of a source row, signs applied: the BF16
+// input itself, or (SILU) the fused activation of a gate/up row [gate | up]
+// (each kdim wide), rounded to BF16 as the unfused SiluAndMul output would be.
+template <bool SILU>
+__device__ __forceinline__ void load8_input(const uint16_t* row, int k, int kdim, uint32_t sbits, float (&v)[8]) {
+  if constexpr (!SILU) {
+    load8_signed(row + k, sbits, v);
+  } else {
+    const uint4 gw = __ldg(reinterpret_cast<const uint4*>(row + k));
+    const uint4 uw = __ldg(reinterpret_cast<const uint4*>(row + kdim + k));
+    const uint32_t gs[4] = {gw.x, gw.y, gw.z, gw.w}, us[4] = {uw.x, uw.y, uw.z, uw.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t h0 = silu_mul_bf16_bits(__uint_as_float(gs[i] << 16), __uint_as_float(us[i] << 16));
+      const uint32_t h1 =
+          silu_mul_bf16_bits(__uint_as_float(gs[i] & 0xFFFF0000u), __uint_as_float(us[i] & 0xFFFF0000u));
+      v[2 * i] = __uint_as_float((h0 << 16) ^ (((sbits >> (2 * i)) & 1u) << 31));
+      v[2 * i + 1] = __uint_as_float((h1 << 16) ^ (((sbits >> (2 * i + 1)) & 1u) << 31));
+    }
+  }
+}
+
 // 8 sign bytes (int8 +-1) -> 8 bits, bit e set for a negative sign.
 __device__ __forceinline__ uint32_t sign_bits8(const int8_t* s) {
   const uint2 w = *reinterpret_cast<const uint2*>(s);
@@ -155,12 +186,12 @@ __device__ __forceinline__ float butterfly_lane(float v, int mask, bool high) {
 
 // ============================================================ block128
 struct Block128Args {
-  const uint16_t* x;
+  const uint16_t* x;  // rows of x_stride elements (K, or 2K for a gate/up source)
   const int8_t* signs;
   uint8_t* packed;   // or nullptr
   int8_t* codes8;    // or nullptr
   uint16_t* scale;
-  int M, K, G, ncb, warps_used, clamp_lo;
+  int M, K, G, ncb, warps_used, clamp_lo, x_stride;
 };
 
 // A warp owns GPW = 32 / LPG consecutive groups (one "column block") of a row;
@@ -169,7 +200,7 @@ struct Block128Args {
 // rest).  Warps keep their column block, and so their signs, while striding
 // over rows.  LPG = 8 halves each lane's work for decode batches; LPG = 4
 // needs fewer shuffles for large batches.
-template <int LPG>
+template <int LPG, bool SILU>
 __global__ void __launch_bounds__(256) rht_block128_kernel(const Block128Args p) {
   constexpr int J = 16 / LPG;    // 8-element register blocks per lane
   constexpr int GPW = 32 / LPG;  // groups per warp
@@ -191,9 +222,9 @@ __global__ void __launch_bounds__(256) rht_block128_kernel(const Block128Args p)
   for (int row = gw / p.ncb; row < p.M; row += row_step) {
     float v[J][8];
     if (active) {
-      const uint16_t* src = p.x + static_cast<size_t>(row) * p.K + g * 128 + l * 8;
+      const uint16_t* src = p.x + static_cast<size_t>(row) * p.x_stride;
 #pragma unroll
-      for (int j = 0; j < J; ++j) load8_signed(src + j * 8 * LPG, sb[j], v[j]);
+      for (int j = 0; j < J; ++j) load8_input<SILU>(src, g * 128 + j * 8 * LPG + l * 8, p.K, sb[j], v[j]);
     } else {
 #pragma unroll
       for (int j = 0; j < J; ++j)
@@ -246,12 +277,12 @@ __global__ void __launch_bounds__(256) rht_block128_kernel(const Block128Args p)
 
 // ============================================================ row_DH
 struct RowDHArgs {
-  const uint16_t* x;
+  const uint16_t* x;  // rows of x_stride elements (K, or 2K for a gate/up source)
   const int8_t* signs;
   uint8_t* packed;   // or nullptr
   int8_t* codes8;    // or nullptr
   uint16_t* scale;
-  int M, clamp_lo;
+  int M, clamp_lo, x_stride;
 };
 
 // Shared-memory index with 4 floats of padding per 32 (keeps float4 accesses
@@ -268,6 +299,7 @@ __device__ __forceinline__ float two_stages(float v0, float v1, float v2, float 
 
 // K = 4096.  Thread (warp w, lane l) holds k = w*1024 + j*256 + l*8 + e:
 // e bits 0-2, lane bits 3-7, j bits 8-9, warp bits 10-11.
+template <bool SILU>
 __global__ void __launch_bounds__(128) rht_rowdh4096_kernel(const RowDHArgs p) {
   grid_dependents_launch();
   constexpr int K = 4096, G = 32;
@@ -280,9 +312,9 @@ __global__ void __launch_bounds__(128) rht_rowdh4096_kernel(const RowDHArgs p) {
 
   for (int row = blockIdx.x; row < p.M; row += gridDim.x) {
     float v[4][8];
-    const uint16_t* src = p.x + static_cast<size_t>(row) * K + w * 1024 + l * 8;
+    const uint16_t* src = p.x + static_cast<size_t>(row) * p.x_stride;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) load8_signed(src + j * 256, sb[j], v[j]);
+    for (int j = 0; j < 4; ++j) load8_input<SILU>(src, w * 1024 + j * 256 + l * 8, K, sb[j], v[j]);
 #pragma unroll
     for (int j = 0; j < 4; ++j) butterfly8(v[j]);
 #pragma unroll
@@ -353,6 +385,7 @@ __device__ __forceinline__ bool h12_positive(int source, int destination) {
 // k = f*1024 + w*256 + l*8 + e: e bits 0-2, lane bits 3-7, warp bits 8-9 of
 // the 1024-point transform; the 12 factors of a position live in one thread,
 // so the H12 mix is register-local.
+template <bool SILU>
 __global__ void __launch_bounds__(128) rht_rowdh12288_kernel(const RowDHArgs p) {
   grid_dependents_launch();
   constexpr int K = 12288, G = 96;
@@ -365,9 +398,9 @@ __global__ void __launch_bounds__(128) rht_rowdh12288_kernel(const RowDHArgs p) 
 
   for (int row = blockIdx.x; row < p.M; row += gridDim.x) {
     float v[12][8];
-    const uint16_t* src = p.x + static_cast<size_t>(row) * K + w * 256 + l * 8;
+    const uint16_t* src = p.x + static_cast<size_t>(row) * p.x_stride;
 #pragma unroll
-    for (int f = 0; f < 12; ++f) load8_signed(src + f * 1024, sb[f], v[f]);
+    for (int f = 0; f < 12; ++f) load8_input<SILU>(src, f * 1024 + w * 256 + l * 8, K, sb[f], v[f]);
 #pragma unroll
     for (int f = 0; f < 12; ++f) butterfly8(v[f]);
 #pragma unroll
@@ -431,9 +464,9 @@ __global__ void __launch_bounds__(128) rht_rowdh12288_kernel(const RowDHArgs p) 
 // ============================================================ host launchers
 constexpr int kRowDH12288Smem = padded(12288) * 4;
 
-// `packed` and/or `codes8` receive the codes (at least one is non-null).
-int launch_rht_quant(const void* x, const void* signs, void* packed, void* codes8, void* scale, int64_t m, int64_t k,
-                     int layout, int clamp_lo, cudaStream_t stream) {
+template <bool SILU>
+static int launch_rht_quant_t(const void* x, const void* signs, void* packed, void* codes8, void* scale, int64_t m,
+                              int64_t k, int layout, int clamp_lo, cudaStream_t stream) {
   const int sms = device_sm_count();
   if (sms <= 0) return NV4_ERR_CUDA;
   if (layout == NV4_LAYOUT_BLOCK128) {
@@ -447,6 +480,7 @@ int launch_rht_quant(const void* x, const void* signs, void* packed, void* codes
     a.K = static_cast<int>(k);
     a.G = static_cast<int>(k / 128);
     a.clamp_lo = clamp_lo;
+    a.x_stride = static_cast<int>(SILU ? 2 * k : k);
     // Decode-sized batches: 8 lanes per group and 4-warp CTAs, so the few rows
     // spread over many SMs with little work per lane; large batches: 4 lanes
     // per group, 8-warp CTAs.
@@ -461,8 +495,8 @@ int launch_rht_quant(const void* x, const void* signs, void* packed, void* codes
     // Programmatic dependent launch: the kernels read only the sign vector before
     // griddepcontrol.wait and write nothing before it, so they may start while
     // the kernel before them in the stream drains.
-    if (small) return launch_kernel(rht_block128_kernel<8>, dim3(blocks), dim3(32 * wpb), 0, stream, true, a);
-    return launch_kernel(rht_block128_kernel<4>, dim3(blocks), dim3(32 * wpb), 0, stream, true, a);
+    if (small) return launch_kernel(rht_block128_kernel<8, SILU>, dim3(blocks), dim3(32 * wpb), 0, stream, true, a);
+    return launch_kernel(rht_block128_kernel<4, SILU>, dim3(blocks), dim3(32 * wpb), 0, stream, true, a);
   }
   RowDHArgs a;
   a.x = static_cast<const uint16_t*>(x);
@@ -472,20 +506,33 @@ int launch_rht_quant(const void* x, const void* signs, void* packed, void* codes
   a.scale = static_cast<uint16_t*>(scale);
   a.M = static_cast<int>(m);
   a.clamp_lo = clamp_lo;
+  a.x_stride = static_cast<int>(SILU ? 2 * k : k);
   if (k == 4096) {
     const int blocks = static_cast<int>(std::min<int64_t>(m, static_cast<int64_t>(sms) * 8));
-    return launch_kernel(rht_rowdh4096_kernel, dim3(blocks), dim3(128), 0, stream, true, a);
+    return launch_kernel(rht_rowdh4096_kernel<SILU>, dim3(blocks), dim3(128), 0, stream, true, a);
   }
   static bool attr_set[64] = {};
   const int dev = current_device();
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    if (cudaFuncSetAttribute(rht_rowdh12288_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(rht_rowdh12288_kernel<SILU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kRowDH12288Smem) != cudaSuccess)
       return NV4_ERR_CUDA;
     attr_set[dev] = true;
   }
   const int blocks = static_cast<int>(std::min<int64_t>(m, static_cast<int64_t>(sms) * 4));
-  return launch_kernel(rht_rowdh12288_kernel, dim3(blocks), dim3(128), kRowDH12288Smem, stream, true, a);
+  return launch_kernel(rht_rowdh12288_kernel<SILU>, dim3(blocks), dim3(128), kRowDH12288Smem, stream, true, a);
+}
+
+// `packed` and/or `codes8` receive the codes (at least one is non-null).
+int launch_rht_quant(const void* x, const void* signs, void* packed, void* codes8, void* scale, int64_t m, int64_t k,
+                     int layout, int clamp_lo, cudaStream_t stream) {
+  return launch_rht_quant_t<false>(x, signs, packed, codes8, scale, m, k, layout, clamp_lo, stream);
+}
+
+// Same, with the prep input computed from a gate/up row [m, 2k] as bf16(silu(gate) * up).
+int launch_silu_mul_rht_quant(const void* gate_up, const void* signs, void* packed, void* codes8, void* scale,
+                              int64_t m, int64_t k, int layout, int clamp_lo, cudaStream_t stream) {
+  return launch_rht_quant_t<true>(gate_up, signs, packed, codes8, scale, m, k, layout, clamp_lo, stream);
 }
 
 }  // namespace nv4

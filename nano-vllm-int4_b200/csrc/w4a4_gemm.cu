@@ -45,6 +45,7 @@
 
 #include "nv4_device.cuh"
 #include "nv4_launch.h"
+#include "peer_common.cuh"
 
 namespace nv4 {
 
@@ -58,6 +59,12 @@ struct StreamGemmArgs {
   int n_iters;    // ceil(G / 2): two groups per stage
   int stages;
   int scale_tma;  // 1: weight scales arrive by TMA (G % 8 == 0, 16-byte aligned rows)
+  // Peer mode (peer_world > 0, FP32 tiles, one token block): CTA j stores its
+  // FP32 tile into inbox[parity][peer_rank] of every rank's peer buffer and
+  // releases flag[peer_rank][j] on the others (peer_common.cuh); `out` is unused.
+  uint8_t* peer_bufs[kPeerMaxRanks];
+  int64_t peer_capacity;
+  int peer_rank, peer_world;
 };
 
 constexpr int kMaxConsumerWarps = 16;
@@ -92,7 +99,7 @@ struct StreamLayout {
     sa_off = (sw_off + sw_bytes + 1023) & ~1023;
     sac_off = (sa_off + MP * G * 2 + 15) & ~15;
     flags_off = sac_off + MP * G * 8;
-    ds_off = (flags_off + 2 * G * 4 + 15) & ~15;  // K-split partials (KS > 1)
+    ds_off = (flags_off + (2 * G + 4) * 4 + 15) & ~15;  // K-split partials (KS > 1)
     bar_off = (ds_off + ds_bytes + 7) & ~7;
     total = bar_off + (2 * S + 2) * 8 + 16;
   }
@@ -124,7 +131,8 @@ __global__ void __launch_bounds__(32 * (kProducerWarps + (KS == 1 && TPW == MT ?
   uint16_t* sa_s = reinterpret_cast<uint16_t*>(smem + L.sa_off);   // [MP][G]
   // [G][MP/2] float4 per token pair (t, t+1): (sa_t/16, sa_t+1/16, -786432*sa_t, -786432*sa_t+1)
   float* sac = reinterpret_cast<float*>(smem + L.sac_off);
-  int* fast_g = reinterpret_cast<int*>(smem + L.flags_off);        // [G]: both scales in range; [G]: some group not
+  int* fast_g = reinterpret_cast<int*>(smem + L.flags_off);        // [G]: both scales in range; [G]: some group not;
+                                                                    // [G + 1]: peer-mode epoch of this call
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
   uint64_t* empty = full + S;
   uint64_t* scale_bar = empty + S;      // weight scales
@@ -240,6 +248,11 @@ __global__ void __launch_bounds__(32 * (kProducerWarps + (KS == 1 && TPW == MT ?
     for (int i = ct; i < R * G; i += cthreads)
       if (!scale_in_fast_range(bf16_bits_to_f32(sw_s[i]), 0x1.0p-30f, 0x1.0p+27f)) fast_g[i % G] = 0, fast_g[G] = 1;
   grid_dependency_wait();
+  if (p.peer_world) {
+    uint8_t* own = p.peer_bufs[p.peer_rank];
+    peer_advance_epochs(own, blockIdx.x, gridDim.x, ct, cthreads);
+    if (ct == 0) fast_g[G + 1] = static_cast<int>(peer_epochs(own)[blockIdx.x]);
+  }
   if (active) {
     // eight independent loads per thread in flight: one L2 round trip for the
     // whole [MP x G] block at decode sizes
@@ -350,12 +363,16 @@ __global__ void __launch_bounds__(32 * (kProducerWarps + (KS == 1 && TPW == MT ?
         }
   };
 
+  const int peer_parity = p.peer_world ? (fast_g[G + 1] & 1) : 0;
   auto store_out = [&](int row, int tok, float v) {
     const int rr = n0 + row, tk = m0 + tok;
     if (tk < p.M && rr < p.N) {
       if (!WG) v = __fmul_rn(v, bf16_bits_to_f32(sw_s[row]));
       const size_t o = static_cast<size_t>(tk) * p.N + rr;
-      if (F32)
+      if (p.peer_world) {
+        for (int r = 0; r < p.peer_world; ++r)
+          peer_inbox(p.peer_bufs[r], p.peer_capacity, peer_parity, p.peer_rank)[o] = v;
+      } else if (F32)
         static_cast<float*>(p.out)[o] = v;
       else
         static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(v);
@@ -435,14 +452,15 @@ __global__ void __launch_bounds__(32 * (kProducerWarps + (KS == 1 && TPW == MT ?
       if (lane == 0) mbar_arrive(&empty[slot]);
     }
 
-    if (!ok) return;  // the producers let their copies land before the CTA exits
+    if (ok) {  // on error the producers let their copies land before the CTA exits
 #pragma unroll
-    for (int t = 0; t < TPW; ++t) {
-      const int t0 = (tile0 + t) * 8 + tig * 2;
-      store_out(row_lo, t0, tot[t][0]);
-      store_out(row_lo, t0 + 1, tot[t][1]);
-      store_out(row_hi, t0, tot[t][2]);
-      store_out(row_hi, t0 + 1, tot[t][3]);
+      for (int t = 0; t < TPW; ++t) {
+        const int t0 = (tile0 + t) * 8 + tig * 2;
+        store_out(row_lo, t0, tot[t][0]);
+        store_out(row_lo, t0 + 1, tot[t][1]);
+        store_out(row_hi, t0, tot[t][2]);
+        store_out(row_hi, t0 + 1, tot[t][3]);
+      }
     }
   } else {
     // K split.  Partials of a block of 2*KS groups (KS stages, one per warp):
@@ -613,11 +631,23 @@ __global__ void __launch_bounds__(32 * (kProducerWarps + (KS == 1 && TPW == MT ?
         }
       }
     }
-    if (error_raised()) return;  // the producers let their copies land before the CTA exits
+    if (!error_raised()) {  // on error the producers let their copies land before the CTA exits
 #pragma unroll
-    for (int o = 0; o < E; ++o) {
-      const int e = ks * E + o, t = e >> 2, i = e & 3;
-      store_out(i < 2 ? row_lo : row_hi, (tile0 + t) * 8 + tig * 2 + (i & 1), tot[o]);
+      for (int o = 0; o < E; ++o) {
+        const int e = ks * E + o, t = e >> 2, i = e & 3;
+        store_out(i < 2 ? row_lo : row_hi, (tile0 + t) * 8 + tig * 2 + (i & 1), tot[o]);
+      }
+    }
+  }
+  if (p.peer_world) {
+    // every consumer's tile stores before one thread's system-scope release of
+    // this CTA's flag on each peer (released on error too, so that the peers
+    // do not wait out their limit; the error word marks the call as failed)
+    named_barrier_sync(1, cthreads);
+    if (ct == 0) {
+      const uint32_t e = static_cast<uint32_t>(fast_g[G + 1]);
+      for (int r = 0; r < p.peer_world; ++r)
+        if (r != p.peer_rank) st_release_sys(peer_flags(p.peer_bufs[r]) + p.peer_rank * kPeerSlots + blockIdx.x, e);
     }
   }
 }
@@ -681,11 +711,11 @@ static bool make_map_u16(CUtensorMap* map, const void* base, uint64_t rows, uint
 // a8 != nullptr: activations in the widened INT8 layout [m, k]; else a_packed [m, k/2].
 int launch_w4a4_stream_gemm(const void* a_packed, const void* a8, const void* w_packed, const void* a_scale,
                             const void* w_scale, void* out, int64_t m, int64_t n, int64_t k, int flags,
-                            cudaStream_t stream) {
+                            cudaStream_t stream, PeerTarget* peer) {
   const int sms = device_sm_count();
   if (sms <= 0) return NV4_ERR_CUDA;
   const bool wg = (flags & NV4_GEMM_W_SCALE_GROUPED) != 0;
-  const bool f32 = (flags & NV4_GEMM_OUT_FP32) != 0;
+  const bool f32 = peer != nullptr || (flags & NV4_GEMM_OUT_FP32) != 0;
   const bool use_a8 = a8 != nullptr;
   const int MT = m <= 8 ? 1 : (m <= 16 ? 2 : 4);
   const int MP = MT * 8;
@@ -748,6 +778,20 @@ int launch_w4a4_stream_gemm(const void* a_packed, const void* a8, const void* w_
   a.stages = stages;
   a.scale_tma = scale_tma ? 1 : 0;
   const dim3 grid(static_cast<unsigned>((n + R - 1) / R), static_cast<unsigned>(mblocks));
+  for (int r = 0; r < kPeerMaxRanks; ++r) a.peer_bufs[r] = nullptr;
+  a.peer_capacity = 0;
+  a.peer_rank = 0;
+  a.peer_world = 0;
+  if (peer) {
+    if (mblocks != 1 || grid.x > static_cast<unsigned>(kPeerSlots) || peer->world < 2 || peer->world > kPeerMaxRanks)
+      return NV4_ERR_UNSUPPORTED;
+    for (int r = 0; r < peer->world; ++r) a.peer_bufs[r] = static_cast<uint8_t*>(peer->bufs[r]);
+    a.peer_capacity = peer->capacity;
+    a.peer_rank = peer->rank;
+    a.peer_world = peer->world;
+    peer->rows_per_cta = R;
+    peer->ctas = static_cast<int>(grid.x);
+  }
   const int threads = 32 * (kProducerWarps + slabs * ts * ks);
   switch (MT * 100 + tpw * 10 + ks) {
     case 111: return launch_flags<1, 1, 1>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);

@@ -36,7 +36,8 @@ GEMM_TC_DECODE = 8
 EXPORTS = ("nv4_rht_quant_pack", "nv4_rht_quant_i8", "nv4_w4a4_grouped_gemm", "nv4_w4a4_gemm_i8", "nv4_w4a4_group_dots", "nv4_w4a16_gemm",
            "nv4_w4a16_workspace_bytes", "nv4_version", "nv4_status_string", "nv4_last_cuda_error",
            "nv4_device_error", "nv4_w4a16_gemm_static", "nv4_peer_header_bytes", "nv4_peer_buffer_alloc",
-           "nv4_peer_buffer_open", "nv4_peer_buffer_close", "nv4_peer_buffer_free", "nv4_peer_allreduce_bf16")
+           "nv4_peer_buffer_open", "nv4_peer_buffer_close", "nv4_peer_buffer_free", "nv4_peer_allreduce_bf16",
+           "nv4_w4a4_gemm_peer_allreduce_bf16", "nv4_silu_mul_rht_quant_i8")
 
 
 class NativeLibraryError(RuntimeError):
@@ -95,6 +96,7 @@ def load(path: str | None = None) -> ctypes.CDLL:
             raise NativeLibraryError(f"failed to load {p}: {e}") from e
         lib.nv4_rht_quant_pack.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _int, _int, _vp]
         lib.nv4_rht_quant_i8.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _int, _int, _vp]
+        lib.nv4_silu_mul_rht_quant_i8.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _int, _int, _vp]
         lib.nv4_w4a4_grouped_gemm.argtypes = [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]
         lib.nv4_w4a4_gemm_i8.argtypes = [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]
         lib.nv4_w4a4_group_dots.argtypes = [_vp, _vp, _vp, _i64, _i64, _i64, _vp]
@@ -109,14 +111,16 @@ def load(path: str | None = None) -> ctypes.CDLL:
         lib.nv4_peer_buffer_close.argtypes = [_vp]
         lib.nv4_peer_buffer_free.argtypes = [_vp]
         lib.nv4_peer_allreduce_bf16.argtypes = [ctypes.POINTER(_vp), _int, _int, _vp, _i64, _i64, _vp]
+        lib.nv4_w4a4_gemm_peer_allreduce_bf16.argtypes = [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int,
+                                                          ctypes.POINTER(_vp), _int, _int, _i64, _vp]
         for name in ("nv4_peer_buffer_alloc", "nv4_peer_buffer_open", "nv4_peer_buffer_close", "nv4_peer_buffer_free",
-                     "nv4_peer_allreduce_bf16"):
+                     "nv4_peer_allreduce_bf16", "nv4_w4a4_gemm_peer_allreduce_bf16"):
             getattr(lib, name).restype = _int
         lib.nv4_w4a16_workspace_bytes.restype = _i64
         lib.nv4_status_string.argtypes = [_int]
         lib.nv4_status_string.restype = ctypes.c_char_p
         lib.nv4_device_error.argtypes = [ctypes.POINTER(_int)]
-        for name in ("nv4_rht_quant_pack", "nv4_rht_quant_i8", "nv4_w4a4_grouped_gemm", "nv4_w4a4_gemm_i8", "nv4_w4a4_group_dots", "nv4_w4a16_gemm",
+        for name in ("nv4_rht_quant_pack", "nv4_rht_quant_i8", "nv4_silu_mul_rht_quant_i8", "nv4_w4a4_grouped_gemm", "nv4_w4a4_gemm_i8", "nv4_w4a4_group_dots", "nv4_w4a16_gemm",
                      "nv4_version", "nv4_last_cuda_error", "nv4_device_error"):
             getattr(lib, name).restype = _int
         if path is None:
@@ -163,6 +167,14 @@ def rht_quant_i8(x, signs, codes, scale, layout: int, clamp_lo: int) -> None:
     with torch.cuda.device(x.device):
         check(load().nv4_rht_quant_i8(ptr(x), ptr(signs), ptr(codes), ptr(scale), m, k, layout, clamp_lo,
                                       stream_of(x)), "nv4_rht_quant_i8")
+
+
+def silu_mul_rht_quant_i8(gate_up, signs, codes, scale, layout: int, clamp_lo: int) -> None:
+    """nv4_silu_mul_rht_quant_i8: the prep of bf16(silu(gate) * up) for gate_up [m, 2k]."""
+    m, k = gate_up.shape[0], gate_up.shape[1] // 2
+    with torch.cuda.device(gate_up.device):
+        check(load().nv4_silu_mul_rht_quant_i8(ptr(gate_up), ptr(signs), ptr(codes), ptr(scale), m, k, layout,
+                                               clamp_lo, stream_of(gate_up)), "nv4_silu_mul_rht_quant_i8")
 
 
 def w4a4_gemm_i8(a_codes, w_packed, a_scale, w_scale, out, flags: int) -> None:
@@ -260,6 +272,21 @@ def w4a4_gemm_i8_to(a_codes, w_packed, a_scale, w_scale, out_addr: int, flags: i
     with torch.cuda.device(a_codes.device):
         check(load().nv4_w4a4_gemm_i8(ptr(a_codes), ptr(w_packed), ptr(a_scale), ptr(w_scale), _vp(out_addr),
                                       m, n, k, flags, stream_of(a_codes)), "nv4_w4a4_gemm_i8")
+
+
+PEER_MAX_TOKENS = 32  # NV4_PEER_MAX_TOKENS
+
+
+def w4a4_gemm_peer_allreduce_bf16(a_codes, w_packed, a_scale, w_scale, out, bufs: list[int], rank: int,
+                                  capacity: int, flags: int) -> None:
+    """Row-parallel GEMM whose CTAs store their FP32 tiles into every rank's
+    inbox, then the rank-order sum to BF16 `out` (nv4_w4a4_gemm_peer_allreduce_bf16)."""
+    m, k, n = a_codes.shape[0], a_codes.shape[1], w_packed.shape[0]
+    arr = (_vp * len(bufs))(*[_vp(b) for b in bufs])
+    with torch.cuda.device(a_codes.device):
+        check(load().nv4_w4a4_gemm_peer_allreduce_bf16(ptr(a_codes), ptr(w_packed), ptr(a_scale), ptr(w_scale),
+                                                       ptr(out), m, n, k, flags, arr, rank, len(bufs), capacity,
+                                                       stream_of(a_codes)), "nv4_w4a4_gemm_peer_allreduce_bf16")
 
 
 def peer_allreduce_bf16(bufs: list[int], rank: int, out, count: int, capacity: int) -> None:

@@ -116,6 +116,33 @@ def rht_quant_i8(x, signs, *, out_codes, out_scale, layout=LAYOUT_VERSION, clamp
     return out_codes, out_scale
 
 
+def silu_mul_rht_quant_i8(gate_up, signs, *, out_codes, out_scale, layout=LAYOUT_VERSION, clamp_lo=-7):
+    """``rht_quant_i8`` of ``SiluAndMul(gate_up)`` in one kernel (the down
+    projection's prep fused with its producer, nanovllm/layers/activation.py:8-11):
+    ``gate_up`` is BF16 [M, 2K] (gate, then up); the prep input
+    bf16(silu(gate) * up) is computed in FP32 with one rounding, as the
+    reference's compiled SiluAndMul, and never written to memory."""
+    lid = _layout_id(layout)
+    if gate_up.ndim != 2 or gate_up.dtype != torch.bfloat16 or gate_up.shape[0] < 1 or gate_up.shape[1] % 2:
+        raise ValueError('Expected BF16 gate_up[M,2K], M>0')
+    m, k = gate_up.shape[0], gate_up.shape[1] // 2
+    if (lid == _native.LAYOUT_ROW_DH and k not in (4096, 12288)) or k % 128 or k < 128:
+        raise ValueError('Unsupported K for this layout')
+    if signs.shape != (k,) or signs.dtype != torch.int8:
+        raise ValueError('Expected INT8 signs[K]')
+    if out_codes.shape != (m, k) or out_codes.dtype != torch.int8:
+        raise ValueError('Expected INT8 codes[M,K]')
+    if out_scale.shape != (m, k // 128) or out_scale.dtype != torch.bfloat16:
+        raise ValueError('Expected BF16 scales[M,K/128]')
+    if any(not t.is_cuda or not t.is_contiguous() or t.device != gate_up.device
+           for t in [gate_up, signs, out_codes, out_scale]):
+        raise ValueError('All tensors must be contiguous on one CUDA device')
+    if clamp_lo not in (-7, -8):
+        raise ValueError('clamp_lo must be -7 or -8')
+    _native.silu_mul_rht_quant_i8(gate_up, signs, out_codes, out_scale, lid, clamp_lo)
+    return out_codes, out_scale
+
+
 def i8_to_codes(codes_i8: torch.Tensor) -> torch.Tensor:
     """Undo the GEMM-ready K order of ``rht_quant_i8`` (for checks): [M, K] codes in k order."""
     m, k = codes_i8.shape

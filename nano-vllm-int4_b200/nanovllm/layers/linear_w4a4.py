@@ -30,7 +30,7 @@ import torch
 import torch.distributed as dist
 from torch import nn
 
-from nanovllm.kernels.rht_a4_tilelang import LAYOUT_VERSION, rht_quant_i8
+from nanovllm.kernels.rht_a4_tilelang import LAYOUT_VERSION, rht_quant_i8, silu_mul_rht_quant_i8
 from nanovllm.kernels.w4a4_grouped_kernel import w4a4_grouped_gemm_i8
 from nanovllm import _native
 
@@ -82,13 +82,34 @@ class W4A4Linear(nn.Module):
                      clamp_lo=self.clamp_lo)
         return codes, scale
 
+    def quantize_silu_mul_input(self, gate_up: torch.Tensor):
+        """The activation prep of SiluAndMul(gate_up) fused with it (the MLP's
+        down projection): gate_up [M, 2K] -> (codes [M,K], scales [M,K/128])."""
+        m = gate_up.shape[0]
+        codes = torch.empty((m, self.in_features), dtype=torch.int8, device=gate_up.device)
+        scale = torch.empty((m, self.in_features // 128), dtype=torch.bfloat16, device=gate_up.device)
+        silu_mul_rht_quant_i8(gate_up, self.signs, out_codes=codes, out_scale=scale, layout=self.layout_id,
+                              clamp_lo=self.clamp_lo)
+        return codes, scale
+
+    def _gemm(self, codes, scale):
+        return w4a4_grouped_gemm_i8(codes, self.packed_weight, scale, self.weight_scale)
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if x.shape[-1] != self.in_features or x.dtype != torch.bfloat16:
             raise ValueError("W4A4Linear requires BF16 activations with the configured input width")
         flat = x.reshape(-1, self.in_features).contiguous()
         codes, scale = self.quantize_input(flat)
-        out = w4a4_grouped_gemm_i8(codes, self.packed_weight, scale, self.weight_scale)
-        return out.reshape(*x.shape[:-1], self.out_features)
+        return self._gemm(codes, scale).reshape(*x.shape[:-1], self.out_features)
+
+    def forward_silu_mul(self, gate_up: torch.Tensor) -> torch.Tensor:
+        """``self(SiluAndMul()(gate_up))`` with the activation fused into the
+        prep (Qwen3MLP.forward's act_fn + down_proj): gate_up BF16 [..., 2K]."""
+        if gate_up.shape[-1] != 2 * self.in_features or gate_up.dtype != torch.bfloat16:
+            raise ValueError("forward_silu_mul requires BF16 gate/up activations of width 2K")
+        flat = gate_up.reshape(-1, 2 * self.in_features).contiguous()
+        codes, scale = self.quantize_silu_mul_input(flat)
+        return self._gemm(codes, scale).reshape(*gate_up.shape[:-1], self.out_features)
 
     @torch.no_grad()
     def load_full(self, packed: torch.Tensor, scale: torch.Tensor, signs: torch.Tensor) -> None:
@@ -236,11 +257,14 @@ class W4A4RowParallelLinear(W4A4Linear):
     """Input dimension K sharded on 128-group boundaries; partial outputs summed
     in FP32 with one all-reduce (linear.py:131-155 pattern).
 
-    Up to PEER_MAX_TOKENS rows the sum is the library's one-shot all-reduce
-    over NVLink peer memory: the GEMM writes its FP32 partial into this rank's
-    peer buffer and one kernel adds every rank's partial in rank order and
-    writes BF16 (about 14 us of NCCL launch and latency per call saved at
-    decode sizes).  The peer buffers are set up on the first forward outside a
+    Up to PEER_MAX_TOKENS rows the sum runs over NVLink peer memory: by
+    default (``fuse_peer_gemm``) the GEMM's CTAs store their FP32 output tiles
+    straight into every rank's inbox and a small kernel adds the ranks' tiles
+    in rank order to BF16; with ``fuse_peer_gemm = False`` the GEMM writes its
+    partial into this rank's peer buffer and the one-shot all-reduce kernel
+    exchanges and sums it.  Both give the same BF16 on every rank and save the
+    NCCL launch and latency (about 14 us per call at decode sizes).  The peer
+    buffers are set up on the first forward outside a
     CUDA-graph capture (one all-gather of IPC handles over the group); if any
     rank cannot set them up, every rank keeps the NCCL all-reduce.  Larger
     batches use NCCL."""
@@ -270,6 +294,7 @@ class W4A4RowParallelLinear(W4A4Linear):
         self.register_buffer("weight_scale", torch.empty(output_size, k_local // 128, dtype=torch.bfloat16))
         self.register_buffer("signs", torch.empty(input_size if self.gather_input else k_local, dtype=torch.int8))
         self.use_peer_allreduce = True
+        self.fuse_peer_gemm = True
 
     def _peer_buffers(self, device):
         """The group's peer buffers, setting them up on first use (collective)."""
@@ -305,13 +330,26 @@ class W4A4RowParallelLinear(W4A4Linear):
             scale = scale_full[:, self.tp_rank * k_local // 128:(self.tp_rank + 1) * k_local // 128].contiguous()
         else:
             codes, scale = self.quantize_input(flat)
+        return self._gemm(codes, scale).reshape(*x.shape[:-1], self.out_features)
+
+    def forward_silu_mul(self, gate_up: torch.Tensor) -> torch.Tensor:
+        if self.gather_input:
+            raise ValueError("forward_silu_mul needs a shard-local layout (block128) or tp_size 1")
+        return W4A4Linear.forward_silu_mul(self, gate_up)
+
+    def _gemm(self, codes, scale):
+        """GEMM of this rank's K shard and the sum over the group (BF16 [M, N])."""
         if self.tp_size == 1:
             out = w4a4_grouped_gemm_i8(codes, self.packed_weight, scale, self.weight_scale)
         else:
             m = codes.shape[0]
             count = m * self.out_features
             peers = self._peer_buffers(codes.device) if m <= self.PEER_MAX_TOKENS else None
-            if peers and count <= PEER_CAPACITY:
+            if peers and count <= PEER_CAPACITY and self.fuse_peer_gemm:
+                out = torch.empty((m, self.out_features), dtype=torch.bfloat16, device=codes.device)
+                _native.w4a4_gemm_peer_allreduce_bf16(codes, self.packed_weight, scale, self.weight_scale, out, peers,
+                                                      self.tp_rank, PEER_CAPACITY, _native.GEMM_W_SCALE_GROUPED)
+            elif peers and count <= PEER_CAPACITY:
                 _native.w4a4_gemm_i8_to(codes, self.packed_weight, scale, self.weight_scale,
                                         peers[self.tp_rank] + _native.peer_header_bytes(),
                                         _native.GEMM_W_SCALE_GROUPED | _native.GEMM_OUT_FP32)
@@ -321,4 +359,4 @@ class W4A4RowParallelLinear(W4A4Linear):
                 partial = w4a4_grouped_gemm_i8(codes, self.packed_weight, scale, self.weight_scale, out_fp32=True)
                 dist.all_reduce(partial, group=self.group)
                 out = partial.to(torch.bfloat16)
-        return out.reshape(*x.shape[:-1], self.out_features)
+        return out

@@ -33,6 +33,12 @@ rounding the reference performs happens here in the same order:
   one FP32 rounding per group, BF16 output.  The FMA is emulated exactly
   (TwoSum in float64 plus a midpoint fix-up), which the reference's
   float64-then-float32 emulation approximates.
+* ``silu_mul_bf16_bits`` -- ``nanovllm/layers/activation.py:8-11``
+  (SiluAndMul under torch.compile): bf16(silu(g) * u) with silu and the
+  product in FP32, one rounding at the end; silu(g) = g / (1 + exp(-g)).
+  numpy's exp and CUDA's expf may differ by an ulp, so this restatement of a
+  transcendental is compared with a tolerance (the GPU path is checked
+  exactly against torch's FP32 arithmetic on the same device).
 * ``w4a16_dequant`` / ``w4a16_gemm`` -- ``nanovllm/layers/linear_w4a16.py:45-59``:
   ``bf16(0x4300 | (w+15-z)) - 144`` times the BF16-rounded FP16 scale, rounded
   to BF16, then an FP32-accumulated GEMM.  The reference has no W4A16 test, so
@@ -199,6 +205,17 @@ def prepare(x_bf16_bits: np.ndarray, signs: np.ndarray, layout: int = LAYOUT_BLO
     r = rotate(x, signs, layout)
     codes, s, q = quantize(r, layout, clamp_lo)
     return pack_int4(codes), f32_to_bf16_bits(s), codes, q, r
+
+
+def silu_mul_bf16_bits(gate_up_bits: np.ndarray) -> np.ndarray:
+    """SiluAndMul of a gate/up BF16 row block [M, 2K] -> BF16 bits [M, K]
+    (activation.py:8-11 as compiled: FP32 silu and product, one rounding)."""
+    gu = bf16_bits_to_f32(gate_up_bits)
+    k = gu.shape[-1] // 2
+    g, u = gu[..., :k], gu[..., k:]
+    with np.errstate(over="ignore"):
+        s = (g / (np.float32(1.0) + np.exp(-g))).astype(np.float32)
+    return f32_to_bf16_bits((s * u).astype(np.float32))
 
 
 def boundary_mask(q: np.ndarray, ulps: int = 1) -> np.ndarray:

@@ -114,3 +114,24 @@ def test_quant_code_shortcut_matches_rounded_quotient():
     ref = np.rint(rn32_quotient(v, s))
     assert np.array_equal(k[~near], ref[~near])
     assert near.sum() > 0        # the adversarial cases reach the IEEE fallback
+
+
+def test_silu_mul_oracle_cpu():
+    """The oracle's SiluAndMul restatement (FP32 silu and product, one BF16
+    rounding) against torch's FP32 arithmetic on the CPU: equal within one BF16
+    ulp (numpy's exp and torch's may differ in the last FP32 bit), with the
+    exact special cases g = 0 -> 0 and a saturated silu(g) = g for large g."""
+    import torch
+    from oracle import nv4_oracle as o
+    g = torch.Generator().manual_seed(0)
+    gu = (torch.randn(16, 2 * 512, generator=g) * 3.0).bfloat16()
+    gu[0, :4] = torch.tensor([0.0, 40.0, -40.0, -100.0]).bfloat16()
+    gu[0, 512:516] = torch.tensor([3.0, 2.0, 5.0, 1.0]).bfloat16()
+    bits = gu.view(torch.int16).numpy().view(np.uint16)
+    got = o.silu_mul_bf16_bits(bits)
+    gf, uf = gu[:, :512].float(), gu[:, 512:].float()
+    want = ((gf / (1.0 + torch.exp(-gf))) * uf).bfloat16().view(torch.int16).numpy().view(np.uint16)
+    diff = np.abs(got.astype(np.int32) - want.astype(np.int32))
+    assert diff.max() <= 1 and (diff == 0).mean() > 0.995
+    vals = o.bf16_bits_to_f32(got[0, :4])
+    assert vals[0] == 0.0 and vals[1] == 80.0 and vals[2] <= 0.0 and abs(vals[3]) == 0.0

@@ -1,5 +1,7 @@
 """Tensor-parallel row-parallel W4A4 layer on every visible GPU (2, 4 or 8;
-NCCL process group): the one-shot peer-memory all-reduce must give the NCCL
+NCCL process group): both peer-memory paths -- the GEMM storing its tiles into
+the peers' inboxes (default) and the GEMM followed by the one-shot all-reduce
+kernel, interleaved on the same peer buffers -- must give the NCCL
 all-reduce's BF16 result -- exactly on 2 ranks (two FP32 partials are added in
 the same order), within BF16 rounding of a different summation order on more
 -- identical on every rank, over repeated calls and CUDA-graph replays, and
@@ -44,9 +46,11 @@ def _worker(rank, world, port, failures):
             scale = (torch.rand(n, k // 128, device=dev, generator=g) * 0.003 + 1e-4).bfloat16()
             signs = torch.randint(0, 2, (k,), dtype=torch.int8, device=dev, generator=g) * 2 - 1
             peer = W4A4RowParallelLinear(k, n, layout=layout, tp_rank=rank, tp_size=world).to(dev)
+            peer2 = W4A4RowParallelLinear(k, n, layout=layout, tp_rank=rank, tp_size=world).to(dev)
+            peer2.fuse_peer_gemm = False
             nccl = W4A4RowParallelLinear(k, n, layout=layout, tp_rank=rank, tp_size=world).to(dev)
             nccl.use_peer_allreduce = False
-            for mod in (peer, nccl):
+            for mod in (peer, peer2, nccl):
                 mod.load_full(packed, scale, signs)
             kl = k // world
 
@@ -57,9 +61,11 @@ def _worker(rank, world, port, failures):
             for m in (1, 32, 33):
                 x = synthetic.activations(m, k, seed=m).to(dev)[:, rank * kl:(rank + 1) * kl].contiguous()
                 want = nccl(x)
-                for _ in range(2):  # repeated calls advance the peer epochs
+                for _ in range(2):  # repeated, interleaved calls advance the peer epochs
                     got = peer(x)
-                    assert same(got, want), (layout, m)
+                    assert same(got, want), (layout, m, "fused")
+                    got2 = peer2(x)
+                    assert torch.equal(got2, got), (layout, m, "two-kernel")
                 every = [torch.empty_like(got) for _ in range(world)]
                 dist.all_gather(every, got)
                 assert all(torch.equal(e, every[0]) for e in every), (layout, m, "ranks differ")
@@ -71,11 +77,13 @@ def _worker(rank, world, port, failures):
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
                 out = peer(x)
+                out2 = peer2(x)
             for seed in (6, 7, 8):
                 x.copy_(synthetic.activations(32, k, seed=seed).to(dev)[:, rank * kl:(rank + 1) * kl])
                 graph.replay()
                 torch.cuda.synchronize()
                 assert same(out, nccl(x)), (layout, seed, "graph replay")
+                assert torch.equal(out2, out), (layout, seed, "graph replay, two-kernel")
             del graph
             graph = None
             torch.cuda.synchronize()
