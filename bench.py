@@ -6,16 +6,21 @@ tokens -- QKV (K=4096 -> N=6144), O (4096 -> 4096), gate/up (4096 -> 24576),
 down (12288 -> 4096) -- each one activation-prep launch (block128 RHT +
 per-group INT4 quantisation + packing, codes in [-8, 7]) and one grouped INT4
 GEMM launch, with distinct random weights per layer (3.58 GB, larger than L2,
-so no flush is needed).  The next projection reads the previous one's output
-(its first M*K elements viewed as [M, K], so no copy kernel sits between
-the projections), as a decoder layer's linears do.  The step is captured
-in a CUDA graph and replayed, as the reference's model runner does for decode.
+so no flush is needed).  The projections are chained as in a Qwen3 decoder
+layer with attention left out (it is not on the quantized-linear path): QKV's
+prep applies the residual add + input RMSNorm, O reads the first M*K elements
+of the QKV output viewed as [M, K] (no copy kernel), gate/up's prep applies
+the residual add + post-attention RMSNorm, and down's prep reads the whole
+gate/up output and applies the MLP's SiluAndMul -- each producer fused into
+the prep kernel, so the norms keep the activations in range as in the model.
+The step is captured in a CUDA graph and replayed, as the reference's model
+runner does for decode.
 
 With ``--gpus N`` (torchrun, one rank per GPU) the layers are tensor-parallel:
 QKV and gate/up split N across ranks, O and down split K on 128-group
-boundaries and sum their FP32 partials with the one-shot peer-memory all-reduce
-kernel over NVLink (one more launch per row-parallel projection; strong
-scaling: the model and batch are fixed).
+boundaries and sum their FP32 partials over NVLink peer memory (the GEMM
+stores its tiles into every rank's inbox and one more launch per row-parallel
+projection sums them; strong scaling: the model and batch are fixed).
 
 ``--impl reference`` times the reference algorithm on the host CPU instead (the
 numpy oracle port of the reference's PyTorch path), on one layer of the same
@@ -47,11 +52,15 @@ SHAPES = [("qkv", 6144, 4096), ("o", 4096, 4096), ("gate_up", 24576, 4096), ("do
 METRIC = "W4A4 decode linears HBM GB/s (Qwen3-8B shapes, batch 32, 36 layers)"
 
 
-def linear_bytes(m: int, n: int, k: int) -> int:
-    """Algorithmic HBM bytes of one prep + GEMM chain: X read, codes (INT8 layout)
-    and scales written then read, weights and weight scales read, BF16 output
+def linear_bytes(m: int, n: int, k: int, silu: bool = False, norm: int = 0) -> int:
+    """Algorithmic HBM bytes of one prep + GEMM chain: X read (the [M, 2K]
+    gate/up output when the prep applies SiluAndMul; with a fused RMSNorm
+    (`norm` = 1) also its BF16 weight, and with the residual add (`norm` = 2)
+    the residual read and the new residual written), codes (INT8 layout) and
+    scales written then read, weights and weight scales read, BF16 output
     written, signs."""
-    prep = 2 * m * k + k + (m * k + 2 * m * k // 128)
+    prep = 2 * m * k * (2 if silu else 1) + k + (m * k + 2 * m * k // 128)
+    prep += (2 * k if norm else 0) + (4 * m * k if norm == 2 else 0)
     return prep + gemm_bytes(m, n, k)
 
 
@@ -61,8 +70,15 @@ def gemm_bytes(m: int, n: int, k: int) -> int:
     return n * k // 2 + 2 * n * k // 128 + m * k + 2 * m * k // 128 + 2 * m * n
 
 
+def layer_bytes(m: int, first: bool) -> int:
+    """One decoder layer of the chain: QKV (RMSNorm, plus the residual add after
+    the first layer), O, gate/up (residual add + RMSNorm), down (SiluAndMul)."""
+    norms = {"qkv": 1 if first else 2, "o": 0, "gate_up": 2, "down": 0}
+    return sum(linear_bytes(m, n, k, silu=name == "down", norm=norms[name]) for name, n, k in SHAPES)
+
+
 def step_bytes(m: int, layers: int) -> int:
-    return layers * sum(linear_bytes(m, n, k) for _, n, k in SHAPES)
+    return layer_bytes(m, True) + (layers - 1) * layer_bytes(m, False)
 
 
 def measured_peaks():
@@ -137,6 +153,9 @@ class ClockSampler(threading.Thread):
 
 
 # ---------------------------------------------------------------- model of the workload
+NORM_EPS = 1e-6
+
+
 def build_layers(device, layers, tp_rank, tp_size):
     from nanovllm.layers.linear_w4a4 import (W4A4MergedColumnParallelLinear, W4A4QKVParallelLinear,
                                              W4A4RowParallelLinear)
@@ -159,6 +178,10 @@ def build_layers(device, layers, tp_rank, tp_size):
             mod.load_full(packed, scale, signs)
             del packed, scale
             layer[name] = mod
+        # input / post-attention RMSNorm weights (around 1, as in trained models)
+        gen.manual_seed(1000 * i + 7)
+        layer["norm_in"] = (1.0 + 0.1 * torch.randn(4096, device=device, generator=gen)).bfloat16()
+        layer["norm_post"] = (1.0 + 0.1 * torch.randn(4096, device=device, generator=gen)).bfloat16()
         mods.append(layer)
     return mods
 
@@ -172,17 +195,24 @@ def head_view(t, k):
 
 
 def forward(mods, x):
-    """Chained decode forward through the linears; x: [32, 4096] BF16 (replicated)."""
-    h = x
+    """Chained decode forward through the linears and their fused producers (a
+    Qwen3 decoder layer without attention); x: [32, 4096] BF16 (replicated)."""
+    h, res = x, None
     for layer in mods:
-        qkv = layer["qkv"](h)
+        qkv, res = layer["qkv"].forward_add_rmsnorm(h, res, layer["norm_in"], NORM_EPS)
         o = layer["o"](head_view(qkv, layer["o"].in_features))
-        gu = layer["gate_up"](o)
-        h = layer["down"](head_view(gu, layer["down"].in_features))
+        gu, res = layer["gate_up"].forward_add_rmsnorm(o, res, layer["norm_post"], NORM_EPS)
+        h = layer["down"].forward_silu_mul(gu)  # SiluAndMul fused into down's prep
     return h
 
 
 # ---------------------------------------------------------------- CPU (oracle port) sample
+def f32_bits(x):
+    """float32 array -> BF16 bit patterns (round to nearest even)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
 def cpu_layer_sample(seed=0):
     """One layer of the chained workload on the host, with the oracle port of the
     reference algorithm (block128, clamp -8).  Returns (seconds, bytes)."""
@@ -197,14 +227,21 @@ def cpu_layer_sample(seed=0):
                         signs.numpy(), codes.numpy()))
     xb = x.view(torch.int16).numpy().view(np.uint16)
 
+    norm_w = f32_bits(np.ones(4096, dtype=np.float32))
+    res0 = xb.copy()
+
     def run():
-        h = xb
-        for (n, k, packed, sbits, signs, codes) in weights:
-            inp = h.reshape(-1)[: h.shape[0] * k].reshape(h.shape[0], k)
-            h = o.w4a4_linear(np.ascontiguousarray(inp), signs, packed, sbits, o.LAYOUT_BLOCK128, -8,
-                              w_codes=codes)
+        h, res = xb, res0
+        for (name, _, _), (n, k, packed, sbits, signs, codes) in zip(SHAPES, weights):
+            if name == "down":
+                inp = o.silu_mul_bf16_bits(h)
+            elif name in ("qkv", "gate_up"):
+                inp, res = o.add_rmsnorm_bf16_bits(h, res, norm_w, NORM_EPS)
+            else:
+                inp = np.ascontiguousarray(h.reshape(-1)[: h.shape[0] * k].reshape(h.shape[0], k))
+            h = o.w4a4_linear(inp, signs, packed, sbits, o.LAYOUT_BLOCK128, -8, w_codes=codes)
         return h
-    return run, sum(linear_bytes(M_TOKENS, n, k) for _, n, k in SHAPES)
+    return run, layer_bytes(M_TOKENS, False)
 
 
 def cpu_baseline(target_s=12.0):
@@ -370,7 +407,8 @@ def main():
             "config": {"workload": "config1-decode-chain", "m_tokens": M_TOKENS, "layers": args.layers,
                        "shapes": {n: [nn, kk] for n, nn, kk in SHAPES}, "layout": "block128", "clamp_lo": -8,
                        "parallelism": f"tp{world}",
-                       "allreduce": (None if world == 1 else "peer-memory one-shot kernel" if peer_ar else "nccl"),
+                       "allreduce": (None if world == 1 else "peer-memory: GEMM tiles into the peers' inboxes, tile sum"
+                                     if peer_ar else "nccl"),
                        "l2": f"weights {weight_bytes / 1e9:.2f} GB per step vs 126 MB L2, no flush",
                        "bytes_per_step": total_bytes},
             "tok_s_linears": M_TOKENS * args.steps / dt,

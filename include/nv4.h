@@ -86,6 +86,23 @@ int nv4_silu_mul_rht_quant_i8(const void* gate_up, const void* signs, void* out_
                               int64_t k, int layout, int clamp_lo, void* stream);
 
 /*
+ * nv4_rht_quant_i8 of the QKV / gate-up input fused with its producer, the
+ * decoder layer's residual add and RMSNorm (nanovllm/layers/layernorm.py:33-45
+ * add_rms_forward; :17-27 rms_forward when residual is NULL):
+ *   xf = f32(x) + f32(residual)                out_residual = bf16(xf)
+ *   h  = bf16(bf16(xf * rsqrtf(mean(xf^2) + eps)) * weight)
+ * then the prep of h (out_codes / out_scale as nv4_rht_quant_i8); h itself is
+ * written to out_normed when that is non-NULL.  The sum of squares is taken in
+ * a fixed order (deterministic; torch's order differs, so h can differ from
+ * torch's in the last BF16 bit).  x, residual, out_residual, out_normed: bf16
+ * [m, k]; weight: bf16 [k]; all 16-byte aligned.  Layouts: block128 with
+ * k % 512 == 0 and k <= 16384, or row_DH with k == 4096.
+ */
+int nv4_add_rmsnorm_rht_quant_i8(const void* x, const void* residual, const void* weight, float eps,
+                                  const void* signs, void* out_codes, void* out_scale, void* out_residual,
+                                  void* out_normed, int64_t m, int64_t k, int layout, int clamp_lo, void* stream);
+
+/*
  * Grouped INT4 GEMM: out[m, n] = sum_g fp32-FMA(dot_g(a, w), sa[m,g] * sw[n,g]),
  * groups of 128 along K in increasing g, one FP32 rounding per group, then BF16.
  * Replaces nanovllm/kernels/w4a4_grouped_kernel.py:104-129 (w4a4_grouped_gemm)

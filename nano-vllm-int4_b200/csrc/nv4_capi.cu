@@ -210,6 +210,22 @@ int nv4_silu_mul_rht_quant_i8(const void* gate_up, const void* signs, void* out_
                                    static_cast<cudaStream_t>(stream));
 }
 
+int nv4_add_rmsnorm_rht_quant_i8(const void* x, const void* residual, const void* weight, float eps,
+                                  const void* signs, void* out_codes, void* out_scale, void* out_residual,
+                                  void* out_normed, int64_t m, int64_t k, int layout, int clamp_lo, void* stream) {
+  const int rc = check_prep_args(x, signs, out_codes, out_scale, m, k, layout, clamp_lo, 16);
+  if (rc != NV4_OK) return rc;
+  if (!weight || (residual && !out_residual) || !(eps >= 0.0f) || !(eps < 1.0f)) return NV4_ERR_INVALID_ARGUMENT;
+  if ((layout == NV4_LAYOUT_BLOCK128 && (k % 512 || k > 16384)) || (layout == NV4_LAYOUT_ROW_DH && k != 4096))
+    return NV4_ERR_UNSUPPORTED;
+  if (!aligned(weight, 16) || (residual && !aligned(residual, 16)) || (out_residual && !aligned(out_residual, 16)) ||
+      (out_normed && !aligned(out_normed, 16)))
+    return NV4_ERR_ALIGNMENT;
+  return launch_add_rmsnorm_rht_quant(x, residual, weight, eps, signs, nullptr, out_codes, out_scale,
+                                      residual ? out_residual : nullptr, out_normed, m, k, layout, clamp_lo,
+                                      static_cast<cudaStream_t>(stream));
+}
+
 static int check_gemm_args(const void* a, const void* w_packed, const void* a_scale, const void* w_scale,
                            const void* out, int64_t m, int64_t n, int64_t k, int flags) {
   if (!a || !w_packed || !a_scale || !w_scale || !out) return NV4_ERR_INVALID_ARGUMENT;

@@ -57,6 +57,11 @@ bool make_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_by
 // Activation prep; `packed` and/or `codes8` (GEMM-ready INT8 layout) receive the codes.
 int launch_rht_quant(const void* x, const void* signs, void* packed, void* codes8, void* scale, int64_t m, int64_t k,
                      int layout, int clamp_lo, cudaStream_t stream);
+// Same, with the input RMSNorm(x + residual) (residual may be null; then out_residual is unused).
+int launch_add_rmsnorm_rht_quant(const void* x, const void* residual, const void* weight, float eps,
+                                 const void* signs, void* packed, void* codes8, void* scale, void* out_residual,
+                                 void* out_normed, int64_t m, int64_t k, int layout, int clamp_lo,
+                                 cudaStream_t stream);
 // Same, with the input bf16(silu(gate) * up) of a gate/up source [m, 2k].
 int launch_silu_mul_rht_quant(const void* gate_up, const void* signs, void* packed, void* codes8, void* scale,
                               int64_t m, int64_t k, int layout, int clamp_lo, cudaStream_t stream);

@@ -37,7 +37,8 @@ EXPORTS = ("nv4_rht_quant_pack", "nv4_rht_quant_i8", "nv4_w4a4_grouped_gemm", "n
            "nv4_w4a16_workspace_bytes", "nv4_version", "nv4_status_string", "nv4_last_cuda_error",
            "nv4_device_error", "nv4_w4a16_gemm_static", "nv4_peer_header_bytes", "nv4_peer_buffer_alloc",
            "nv4_peer_buffer_open", "nv4_peer_buffer_close", "nv4_peer_buffer_free", "nv4_peer_allreduce_bf16",
-           "nv4_w4a4_gemm_peer_allreduce_bf16", "nv4_silu_mul_rht_quant_i8")
+           "nv4_w4a4_gemm_peer_allreduce_bf16", "nv4_silu_mul_rht_quant_i8",
+           "nv4_add_rmsnorm_rht_quant_i8")
 
 
 class NativeLibraryError(RuntimeError):
@@ -97,6 +98,8 @@ def load(path: str | None = None) -> ctypes.CDLL:
         lib.nv4_rht_quant_pack.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _int, _int, _vp]
         lib.nv4_rht_quant_i8.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _int, _int, _vp]
         lib.nv4_silu_mul_rht_quant_i8.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _int, _int, _vp]
+        lib.nv4_add_rmsnorm_rht_quant_i8.argtypes = [_vp, _vp, _vp, ctypes.c_float, _vp, _vp, _vp, _vp, _vp, _i64,
+                                                     _i64, _int, _int, _vp]
         lib.nv4_w4a4_grouped_gemm.argtypes = [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]
         lib.nv4_w4a4_gemm_i8.argtypes = [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]
         lib.nv4_w4a4_group_dots.argtypes = [_vp, _vp, _vp, _i64, _i64, _i64, _vp]
@@ -120,7 +123,8 @@ def load(path: str | None = None) -> ctypes.CDLL:
         lib.nv4_status_string.argtypes = [_int]
         lib.nv4_status_string.restype = ctypes.c_char_p
         lib.nv4_device_error.argtypes = [ctypes.POINTER(_int)]
-        for name in ("nv4_rht_quant_pack", "nv4_rht_quant_i8", "nv4_silu_mul_rht_quant_i8", "nv4_w4a4_grouped_gemm", "nv4_w4a4_gemm_i8", "nv4_w4a4_group_dots", "nv4_w4a16_gemm",
+        for name in ("nv4_rht_quant_pack", "nv4_rht_quant_i8", "nv4_silu_mul_rht_quant_i8",
+                     "nv4_add_rmsnorm_rht_quant_i8", "nv4_w4a4_grouped_gemm", "nv4_w4a4_gemm_i8", "nv4_w4a4_group_dots", "nv4_w4a16_gemm",
                      "nv4_version", "nv4_last_cuda_error", "nv4_device_error"):
             getattr(lib, name).restype = _int
         if path is None:
@@ -175,6 +179,18 @@ def silu_mul_rht_quant_i8(gate_up, signs, codes, scale, layout: int, clamp_lo: i
     with torch.cuda.device(gate_up.device):
         check(load().nv4_silu_mul_rht_quant_i8(ptr(gate_up), ptr(signs), ptr(codes), ptr(scale), m, k, layout,
                                                clamp_lo, stream_of(gate_up)), "nv4_silu_mul_rht_quant_i8")
+
+
+def add_rmsnorm_rht_quant_i8(x, residual, weight, eps: float, signs, codes, scale, out_residual, out_normed,
+                             layout: int, clamp_lo: int) -> None:
+    """nv4_add_rmsnorm_rht_quant_i8 (residual, out_residual, out_normed may be None)."""
+    m, k = x.shape
+    with torch.cuda.device(x.device):
+        check(load().nv4_add_rmsnorm_rht_quant_i8(ptr(x), _vp(0) if residual is None else ptr(residual), ptr(weight),
+                                                  float(eps), ptr(signs), ptr(codes), ptr(scale),
+                                                  _vp(0) if out_residual is None else ptr(out_residual),
+                                                  _vp(0) if out_normed is None else ptr(out_normed), m, k, layout,
+                                                  clamp_lo, stream_of(x)), "nv4_add_rmsnorm_rht_quant_i8")
 
 
 def w4a4_gemm_i8(a_codes, w_packed, a_scale, w_scale, out, flags: int) -> None:

@@ -143,6 +143,43 @@ def silu_mul_rht_quant_i8(gate_up, signs, *, out_codes, out_scale, layout=LAYOUT
     return out_codes, out_scale
 
 
+def add_rmsnorm_rht_quant_i8(x, residual, weight, eps, signs, *, out_codes, out_scale, out_residual=None,
+                             out_normed=None, layout=LAYOUT_VERSION, clamp_lo=-7):
+    """``rht_quant_i8`` of ``RMSNorm(x + residual)`` in one kernel (the QKV /
+    gate-up prep fused with the decoder layer's add + RMSNorm,
+    nanovllm/layers/layernorm.py:33-45; ``residual=None`` is rms_forward).
+    Writes the new residual bf16(x + residual) to ``out_residual`` (required
+    with a residual) and, if given, the normalized BF16 activation to
+    ``out_normed``.  Returns ``(out_codes, out_scale)``."""
+    lid = _layout_id(layout)
+    if x.ndim != 2 or x.dtype != torch.bfloat16 or x.shape[0] < 1:
+        raise ValueError('Expected BF16 X[M,K], M>0')
+    m, k = x.shape
+    if (lid == _native.LAYOUT_ROW_DH and k != 4096) or (lid == _native.LAYOUT_BLOCK128 and (k % 512 or k > 16384)):
+        raise ValueError('Unsupported K for this layout')
+    for name, t in (('residual', residual), ('out_residual', out_residual), ('out_normed', out_normed)):
+        if t is not None and (t.shape != (m, k) or t.dtype != torch.bfloat16):
+            raise ValueError(f'Expected BF16 {name}[M,K]')
+    if residual is not None and out_residual is None:
+        raise ValueError('out_residual is required with a residual')
+    if weight.shape != (k,) or weight.dtype != torch.bfloat16:
+        raise ValueError('Expected BF16 weight[K]')
+    if signs.shape != (k,) or signs.dtype != torch.int8:
+        raise ValueError('Expected INT8 signs[K]')
+    if out_codes.shape != (m, k) or out_codes.dtype != torch.int8:
+        raise ValueError('Expected INT8 codes[M,K]')
+    if out_scale.shape != (m, k // 128) or out_scale.dtype != torch.bfloat16:
+        raise ValueError('Expected BF16 scales[M,K/128]')
+    ts = [t for t in (x, residual, weight, signs, out_codes, out_scale, out_residual, out_normed) if t is not None]
+    if any(not t.is_cuda or not t.is_contiguous() or t.device != x.device for t in ts):
+        raise ValueError('All tensors must be contiguous on one CUDA device')
+    if clamp_lo not in (-7, -8):
+        raise ValueError('clamp_lo must be -7 or -8')
+    _native.add_rmsnorm_rht_quant_i8(x, residual, weight, eps, signs, out_codes, out_scale, out_residual, out_normed,
+                                     lid, clamp_lo)
+    return out_codes, out_scale
+
+
 def i8_to_codes(codes_i8: torch.Tensor) -> torch.Tensor:
     """Undo the GEMM-ready K order of ``rht_quant_i8`` (for checks): [M, K] codes in k order."""
     m, k = codes_i8.shape

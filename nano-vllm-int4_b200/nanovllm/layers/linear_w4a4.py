@@ -30,7 +30,8 @@ import torch
 import torch.distributed as dist
 from torch import nn
 
-from nanovllm.kernels.rht_a4_tilelang import LAYOUT_VERSION, rht_quant_i8, silu_mul_rht_quant_i8
+from nanovllm.kernels.rht_a4_tilelang import (LAYOUT_VERSION, add_rmsnorm_rht_quant_i8, rht_quant_i8,
+                                               silu_mul_rht_quant_i8)
 from nanovllm.kernels.w4a4_grouped_kernel import w4a4_grouped_gemm_i8
 from nanovllm import _native
 
@@ -101,6 +102,24 @@ class W4A4Linear(nn.Module):
         flat = x.reshape(-1, self.in_features).contiguous()
         codes, scale = self.quantize_input(flat)
         return self._gemm(codes, scale).reshape(*x.shape[:-1], self.out_features)
+
+    def forward_add_rmsnorm(self, x: torch.Tensor, residual, norm_weight: torch.Tensor, eps: float = 1e-6):
+        """``self(RMSNorm(x + residual))`` with the decoder layer's add + RMSNorm
+        fused into the prep (layernorm.py:33-45, then this projection): returns
+        ``(output, new_residual)`` with new_residual = bf16(x + residual), or
+        ``(output, x)`` when ``residual`` is None (rms_forward on x)."""
+        if x.shape[-1] != self.in_features or x.dtype != torch.bfloat16:
+            raise ValueError("forward_add_rmsnorm requires BF16 activations with the configured input width")
+        flat = x.reshape(-1, self.in_features).contiguous()
+        m = flat.shape[0]
+        codes = torch.empty((m, self.in_features), dtype=torch.int8, device=flat.device)
+        scale = torch.empty((m, self.in_features // 128), dtype=torch.bfloat16, device=flat.device)
+        res = None if residual is None else residual.reshape(-1, self.in_features).contiguous()
+        new_res = torch.empty_like(flat) if res is not None else None
+        add_rmsnorm_rht_quant_i8(flat, res, norm_weight, eps, self.signs, out_codes=codes, out_scale=scale,
+                                 out_residual=new_res, layout=self.layout_id, clamp_lo=self.clamp_lo)
+        out = self._gemm(codes, scale).reshape(*x.shape[:-1], self.out_features)
+        return out, (x if new_res is None else new_res.reshape(x.shape))
 
     def forward_silu_mul(self, gate_up: torch.Tensor) -> torch.Tensor:
         """``self(SiluAndMul()(gate_up))`` with the activation fused into the

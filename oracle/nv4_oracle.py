@@ -39,6 +39,11 @@ rounding the reference performs happens here in the same order:
   numpy's exp and CUDA's expf may differ by an ulp, so this restatement of a
   transcendental is compared with a tolerance (the GPU path is checked
   exactly against torch's FP32 arithmetic on the same device).
+* ``add_rmsnorm_bf16_bits`` -- ``nanovllm/layers/layernorm.py:33-45``
+  (add_rms_forward; rms_forward without a residual): FP32 sum, BF16 residual,
+  var = mean(xf^2), bf16(bf16(xf * rsqrt(var + eps)) * weight).  The order of
+  the FP32 reduction is numpy's, so this restatement is compared with a
+  tolerance.
 * ``w4a16_dequant`` / ``w4a16_gemm`` -- ``nanovllm/layers/linear_w4a16.py:45-59``:
   ``bf16(0x4300 | (w+15-z)) - 144`` times the BF16-rounded FP16 scale, rounded
   to BF16, then an FP32-accumulated GEMM.  The reference has no W4A16 test, so
@@ -216,6 +221,19 @@ def silu_mul_bf16_bits(gate_up_bits: np.ndarray) -> np.ndarray:
     with np.errstate(over="ignore"):
         s = (g / (np.float32(1.0) + np.exp(-g))).astype(np.float32)
     return f32_to_bf16_bits((s * u).astype(np.float32))
+
+
+def add_rmsnorm_bf16_bits(x_bits: np.ndarray, residual_bits, weight_bits: np.ndarray, eps: float = 1e-6):
+    """RMSNorm(x + residual) of BF16 rows (layernorm.py:33-45) -> (normed bits,
+    new residual bits); residual None is rms_forward (the residual is x)."""
+    xf = bf16_bits_to_f32(x_bits)
+    if residual_bits is not None:
+        xf = (xf + bf16_bits_to_f32(residual_bits)).astype(np.float32)
+    var = np.mean(xf * xf, axis=-1, keepdims=True, dtype=np.float32)
+    r = (np.float32(1.0) / np.sqrt(var + np.float32(eps))).astype(np.float32)
+    y = round_to_bf16((xf * r).astype(np.float32))
+    h = f32_to_bf16_bits((y * bf16_bits_to_f32(weight_bits)).astype(np.float32))
+    return h, f32_to_bf16_bits(xf)
 
 
 def boundary_mask(q: np.ndarray, ulps: int = 1) -> np.ndarray:
