@@ -208,8 +208,11 @@ __global__ void __launch_bounds__(32 * (kProducerWarps + (KS == 1 && TPW == MT ?
         last = it;
       }
       if (error_raised()) {
-        // Before the CTA may exit, the copies this thread issued must have landed.
+        // Before the CTA may exit, the copies this thread issued must have
+        // landed: its stages, and (warp 0) the weight scales, which consumers
+        // that gave up may not have waited for.
         for (int it = last; it >= 0 && it > last - S; it -= kProducerWarps) mbar_wait_drain(&full[it % S], (it / S) & 1);
+        if (pw == 0 && p.scale_tma) mbar_wait_drain(&scale_bar[0], 0);
       }
     }
     return;
