@@ -729,25 +729,38 @@ int launch_w4a4_stream_gemm(const void* a_packed, const void* a8, const void* w_
   const int64_t ctas_per_mblock = std::max<int64_t>(1, sms / std::min<int64_t>(mblocks, sms));
   int slabs = static_cast<int>(std::min<int64_t>(kMaxConsumerWarps, (total_slabs + ctas_per_mblock - 1) / ctas_per_mblock));
   slabs = std::max(1, slabs);
-  // Narrow layers (few slabs per CTA): split K over 4 (up to 4 slabs) or 2 (up
-  // to 8) warps per slab, and with 32 tokens and at most 2 slabs also split the
-  // token tiles over two warps (16 consumer warps).  Wider ones: split token
-  // tiles over two warps per slab when that still fits (each widens the slab's
-  // weights, so no further).
-  const int ks = slabs <= 4 ? 4 : (slabs <= 8 ? 2 : 1);
-  if (ks == 1) slabs = std::min(slabs, kMaxWideSlabs);  // wider layers take more CTAs
-  int ts = (ks == 4 && MT == 4 && slabs <= 2) ? 2 : 1;
-  if (ks == 1 && MT >= 2 && slabs * 2 <= kMaxConsumerWarps && slabs < 8) ts = 2;
-  const int tpw = MT / ts;
-  const int ds_bytes = stream_ds_bytes(slabs * ts, ks, tpw);
-  const int R = slabs * 16;
+  // Narrow layers (up to 4 slabs per CTA): split K over 4 warps per slab, and
+  // with 32 tokens and at most 2 slabs also split the token tiles over two
+  // warps (16 consumer warps).  5-8 slabs take 4-slab CTAs (more CTAs than
+  // SMs) rather than a 2-way K split.  Wider ones: one warp per slab.
+  //
+  // Ring rule.  A producer warp reuses a slot after waiting on its empty
+  // barrier by phase parity, which is only sound if the slot's previous phase
+  // has completed.  Producers issue stages round-robin (kProducerWarps of
+  // them) and, with a K split, the KS warps of a block release their stages in
+  // any order, so the ring must hold KS + kProducerWarps stages (or all of K):
+  // with fewer, a producer can pass the wait one phase early and a TMA copy
+  // can overwrite a slot still being read.  Fewer slabs per CTA until it fits.
+  if (slabs > 4 && slabs <= 8) slabs = 4;
   const int n_iters = (G + 1) / 2;
   const bool scale_tma = (G % 8) == 0 && (reinterpret_cast<uintptr_t>(w_scale) & 15) == 0;
-  const StreamLayout one(R, MP, G, 1, wg, ds_bytes);
-  const int fixed = one.total - one.stage_bytes;
-  int stages = (kSmemLimit - 1024 - fixed - 64) / (one.stage_bytes + 16);
-  stages = std::min(stages, std::min(16, n_iters));
-  if (stages < 1) return NV4_ERR_UNSUPPORTED;
+  int ks = 0, ts = 1, tpw = MT, ds_bytes = 0, R = 0, stages = 0;
+  for (;;) {
+    ks = slabs <= 4 ? 4 : 1;
+    if (ks == 1) slabs = std::min(slabs, kMaxWideSlabs);  // wider layers take more CTAs
+    ts = (ks == 4 && MT == 4 && slabs <= 2) ? 2 : 1;
+    if (ks == 1 && MT >= 2 && slabs * 2 <= kMaxConsumerWarps && slabs < 8) ts = 2;
+    tpw = MT / ts;
+    ds_bytes = stream_ds_bytes(slabs * ts, ks, tpw);
+    R = slabs * 16;
+    const StreamLayout one(R, MP, G, 1, wg, ds_bytes);
+    const int fixed = one.total - one.stage_bytes;
+    stages = (kSmemLimit - 1024 - fixed - 64) / (one.stage_bytes + 16);
+    stages = std::min(stages, std::min(16, n_iters));
+    if (stages >= std::min(n_iters, ks + kProducerWarps) || slabs == 1) break;
+    slabs = slabs > 4 ? 4 : slabs - 1;
+  }
+  if (stages < 1 || stages < std::min(n_iters, ks + kProducerWarps)) return NV4_ERR_UNSUPPORTED;
   const StreamLayout lay(R, MP, G, stages, wg, ds_bytes);
   const int smem = lay.total + 1024;
 
@@ -798,16 +811,13 @@ int launch_w4a4_stream_gemm(const void* a_packed, const void* a8, const void* w_
   const int threads = 32 * (kProducerWarps + slabs * ts * ks);
   switch (MT * 100 + tpw * 10 + ks) {
     case 111: return launch_flags<1, 1, 1>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
-    case 112: return launch_flags<1, 1, 2>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
     case 114: return launch_flags<1, 1, 4>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
     case 211: return launch_flags<2, 1, 1>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
     case 221: return launch_flags<2, 2, 1>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
-    case 222: return launch_flags<2, 2, 2>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
     case 224: return launch_flags<2, 2, 4>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
     case 411: return launch_flags<4, 1, 1>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
     case 421: return launch_flags<4, 2, 1>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
     case 441: return launch_flags<4, 4, 1>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
-    case 442: return launch_flags<4, 4, 2>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
     case 424: return launch_flags<4, 2, 4>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
     case 444: return launch_flags<4, 4, 4>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
     default: return NV4_ERR_UNSUPPORTED;
