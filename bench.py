@@ -20,10 +20,9 @@ With ``--gpus N`` (torchrun, one rank per GPU) every rank runs the same chain
 on its own batch of 32 with its own copy of the weights -- data-parallel
 decode replicas, weak scaling, the device time taken as the maximum over
 ranks.  The tensor-parallel layers (``W4A4*ParallelLinear`` with the
-peer-memory row-parallel sum) are tested for parity on 2-4 GPUs but are not
-benchmarked here: the 36-layer tensor-parallel chain has shown an
-intermittent launch failure with asynchronous launches that is not
-root-caused.
+peer-memory row-parallel sum) are tested for parity on 2-4 GPUs, and the
+36-layer TP=2 chain has run clean; they are not benchmarked here until the
+TP=4 and TP=8 chains have been run end to end as well.
 
 ``--impl reference`` times the reference algorithm on the host CPU instead (the
 numpy oracle port of the reference's PyTorch path), on one layer of the same
