@@ -157,3 +157,22 @@ def test_base_config_mismatch_rejected(checkpoint):
     (base / "config.json").write_text(json.dumps({"hidden_size": HIDDEN + 1}))
     with pytest.raises(ValueError, match="Base model config"):
         loader_w4a4.load_w4a4_model(_Model(), str(base), str(ckpt))
+
+
+@pytest.mark.parametrize("what", ["scale", "signs"])
+def test_invalid_values_rejected(checkpoint, what):
+    base, ckpt, tensors = checkpoint
+    t = dict(tensors[0])
+    if what == "scale":
+        t["mlp.up_proj.scale"] = t["mlp.up_proj.scale"].clone()
+        t["mlp.up_proj.scale"][3, 0] = 0
+    else:
+        t["signs.o"] = t["signs.o"].clone()
+        t["signs.o"][5] = 2
+    path = ckpt / "layer_0.safetensors"
+    save_file(t, str(path))
+    manifest = json.loads((ckpt / "manifest.json").read_text())
+    manifest["layers"]["0"]["sha256"] = _sha(path)
+    (ckpt / "manifest.json").write_text(json.dumps(manifest))
+    with pytest.raises(ValueError, match="Invalid weight/scale" if what == "scale" else "Invalid RHT signs"):
+        loader_w4a4.load_w4a4_model(_Model(), str(base), str(ckpt))
