@@ -41,7 +41,6 @@ extern "C" {
 #define NV4_GEMM_W_SCALE_GROUPED 1 /* w_scale is bf16 [N, K/128]; otherwise bf16 [N] */
 #define NV4_GEMM_OUT_FP32 2        /* out is float32 [M, N] (diagnostic); otherwise bf16 */
 #define NV4_GEMM_FORCE_STREAM 4    /* always use the weight-streaming mma.sync kernel (tests) */
-#define NV4_GEMM_TC_DECODE 8       /* m <= 32: tcgen05 decode kernel (weights widened into TMEM) */
 
 /*
  * Randomized Hadamard transform, per-128-group activation quantisation and

@@ -104,25 +104,17 @@ bool make_tensor_map_u8(CUtensorMap* map, const void* base, uint64_t rows, uint6
 int launch_w4a4_tc_gemm(const void* a8, const void* w_packed, const void* a_scale, const void* w_scale, void* out,
                         int64_t m, int64_t n, int64_t k, int flags, cudaStream_t stream);
 
-int launch_w4a4_tcd_gemm(const void* a8, const void* w_packed, const void* a_scale, const void* w_scale, void* out,
-                         int64_t m, int64_t n, int64_t k, int flags, cudaStream_t stream);
-
 // Dispatch of the INT8-layout activation path: more than kTcMinTokens tokens go
 // to the tiled tcgen05 kernel (tensor-bound prefill shapes); fewer, packed
 // activations and NV4_GEMM_FORCE_STREAM to the mma.sync weight-streaming
-// kernel.  NV4_GEMM_TC_DECODE sends up to kTcdMaxTokens tokens to the decode
-// tcgen05 kernel instead (weights widened into TMEM); at these sizes an MMA
-// instruction covers 128 weight rows but only 8-32 tokens, and on B200 that
-// kernel is still slower than the streaming one, so it is opt-in.
+// kernel.  (At 8-32 tokens one tcgen05 MMA covers 128 weight rows but only the
+// few tokens, and its issue cost leaves it no faster than mma.sync there.)
 constexpr int64_t kTcMinTokens = 64;
-constexpr int64_t kTcdMaxTokens = 32;
 
 int launch_w4a4_gemm(const void* a_packed, const void* a8, const void* w_packed, const void* a_scale,
                      const void* w_scale, void* out, int64_t m, int64_t n, int64_t k, int flags, cudaStream_t stream) {
-  const bool tcd = (flags & NV4_GEMM_TC_DECODE) != 0 && m <= kTcdMaxTokens;
-  if (a8 != nullptr && !(flags & NV4_GEMM_FORCE_STREAM) && (m > kTcMinTokens || tcd)) {
-    const int rc = m > kTcMinTokens ? launch_w4a4_tc_gemm(a8, w_packed, a_scale, w_scale, out, m, n, k, flags, stream)
-                                    : launch_w4a4_tcd_gemm(a8, w_packed, a_scale, w_scale, out, m, n, k, flags, stream);
+  if (a8 != nullptr && !(flags & NV4_GEMM_FORCE_STREAM) && m > kTcMinTokens) {
+    const int rc = launch_w4a4_tc_gemm(a8, w_packed, a_scale, w_scale, out, m, n, k, flags, stream);
     if (rc != NV4_ERR_UNSUPPORTED) return rc;
   }
   return launch_w4a4_stream_gemm(a_packed, a8, w_packed, a_scale, w_scale, out, m, n, k, flags, stream);
@@ -232,7 +224,7 @@ static int check_gemm_args(const void* a, const void* w_packed, const void* a_sc
   if (m < 1 || n < 1 || k < 128 || k % 128 || n % 8 || m > (int64_t(1) << 31) - 1 || n > (int64_t(1) << 31) - 1 ||
       k > (int64_t(1) << 24))
     return NV4_ERR_INVALID_ARGUMENT;
-  if (flags & ~(NV4_GEMM_W_SCALE_GROUPED | NV4_GEMM_OUT_FP32 | NV4_GEMM_FORCE_STREAM | NV4_GEMM_TC_DECODE))
+  if (flags & ~(NV4_GEMM_W_SCALE_GROUPED | NV4_GEMM_OUT_FP32 | NV4_GEMM_FORCE_STREAM))
     return NV4_ERR_INVALID_ARGUMENT;
   if (!aligned(a, 16) || !aligned(w_packed, 16) || !aligned(a_scale, 2) || !aligned(w_scale, 2) ||
       !aligned(out, (flags & NV4_GEMM_OUT_FP32) ? 4 : 2))

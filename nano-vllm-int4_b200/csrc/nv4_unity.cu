@@ -3,6 +3,5 @@
 #include "rht_quant.cu"
 #include "w4a4_gemm.cu"
 #include "w4a4_gemm_tc.cu"
-#include "w4a4_gemm_tcd.cu"
 #include "w4a16_gemm.cu"
 #include "peer_allreduce.cu"

@@ -53,11 +53,17 @@ __device__ __forceinline__ float round_scale(float s, uint16_t* bits) {
   return __bfloat162float(b);
 }
 
-// x / fl32(sqrt(128)), correctly rounded: q0 = x*r, then one Newton-style
-// correction with the exact residual fma(-q0, d, x).  For this divisor the
-// result equals the IEEE quotient for every significand once |x| >= 2^-100
-// (checked exhaustively on the host, tests/test_prep_arith_cpu.py); below that
-// the intermediates may be subnormal and the IEEE division is used.
+// x / fl32(sqrt(128)), correctly rounded: q0 = x*r with r = RN(1/d), then one
+// residual correction q1 = fma(fma(-q0, d, x), r, q0) -- Markstein's
+// correction step (P. Markstein, "Computation of elementary functions on the
+// IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990), used here in
+// the setting of a divisor known in advance studied by N. Brisebarre,
+// J.-M. Muller and S. K. Raina ("Accelerating correctly rounded floating-point
+// division when the divisor is known in advance", IEEE Trans. Computers 53(8),
+// 2004).  For this divisor the result equals the IEEE quotient for every
+// significand once |x| >= 2^-100 (checked exhaustively on the host,
+// tests/test_prep_arith_cpu.py); below that the intermediates may be subnormal
+// and the IEEE division is used.
 __device__ __forceinline__ float div_sqrt128(float x) {
   const float q0 = x * kInvSqrt128;
   const float q1 = fmaf(fmaf(-q0, kSqrt128, x), kInvSqrt128, q0);

@@ -31,7 +31,6 @@ LAYOUTS = {"block128": LAYOUT_BLOCK128, "row_DH_paley12_kron_sylvester_v1": LAYO
 GEMM_W_SCALE_GROUPED = 1
 GEMM_OUT_FP32 = 2
 GEMM_FORCE_STREAM = 4
-GEMM_TC_DECODE = 8
 
 EXPORTS = ("nv4_rht_quant_pack", "nv4_rht_quant_i8", "nv4_w4a4_grouped_gemm", "nv4_w4a4_gemm_i8", "nv4_w4a4_group_dots", "nv4_w4a16_gemm",
            "nv4_w4a16_workspace_bytes", "nv4_version", "nv4_status_string", "nv4_last_cuda_error",

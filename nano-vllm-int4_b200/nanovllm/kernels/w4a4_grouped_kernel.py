@@ -105,13 +105,11 @@ def w4a4_grouped_gemm(a_packed, w_packed, a_scale, w_scale, out=None, config=Non
     return out
 
 
-def w4a4_grouped_gemm_i8(a_codes, w_packed, a_scale, w_scale, out=None, *, out_fp32=False, force_stream=False,
-                         tc_decode=False):
+def w4a4_grouped_gemm_i8(a_codes, w_packed, a_scale, w_scale, out=None, *, out_fp32=False, force_stream=False):
     """``w4a4_grouped_gemm`` with activations as the INT8 [M, K] codes written by
     ``rht_quant_i8`` (same results; used by the linear layers).  More than 64
     tokens run on the tcgen05 kernel, fewer on the mma.sync weight-streaming
-    kernel; ``force_stream=True`` selects the latter for any size, and
-    ``tc_decode=True`` the tcgen05 decode kernel for up to 32 tokens."""
+    kernel; ``force_stream=True`` selects the latter for any size."""
     if a_codes.ndim != 2 or w_packed.ndim != 2 or a_codes.shape[1] != w_packed.shape[1] * 2:
         raise ValueError("Require INT8 codes [M,K] and packed weights [N,K/2]")
     if a_codes.dtype != torch.int8 or w_packed.dtype != torch.int8:
@@ -136,8 +134,6 @@ def w4a4_grouped_gemm_i8(a_codes, w_packed, a_scale, w_scale, out=None, *, out_f
     flags = (_native.GEMM_W_SCALE_GROUPED if weight_grouped else 0) | (_native.GEMM_OUT_FP32 if out_fp32 else 0)
     if force_stream:
         flags |= _native.GEMM_FORCE_STREAM
-    if tc_decode:
-        flags |= _native.GEMM_TC_DECODE
     _native.w4a4_gemm_i8(a_codes, w_packed, a_scale, w_scale, out, flags)
     return out
 

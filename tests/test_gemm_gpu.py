@@ -132,7 +132,7 @@ def test_extreme_scales(cuda_device):
     np.testing.assert_array_equal(got32.numpy(), oracle_out(qa, qw, sa, sw))
 
 
-@pytest.mark.parametrize("path", ["default", "mma_sync", "tc_decode"])
+@pytest.mark.parametrize("path", ["default", "mma_sync"])
 @pytest.mark.parametrize("grouped", [True, False])
 @pytest.mark.parametrize("m,n,k", [(1, 6144, 4096), (8, 4096, 4096), (32, 24576, 4096), (32, 4096, 12288),
                                    (17, 96, 512), (33, 136, 4096), (100, 64, 2048), (5, 24, 384),
@@ -144,7 +144,7 @@ def test_extreme_scales(cuda_device):
 def test_i8_activation_gemm_exact(cuda_device, m, n, k, grouped, path):
     """nv4_w4a4_gemm_i8 (the path W4A4Linear uses) equals the oracle bit for bit
     on every kernel: the default dispatch (tcgen05 above 64 tokens, mma.sync
-    below), the mma.sync kernel forced, and the tcgen05 decode kernel."""
+    below) and the mma.sync kernel forced."""
     from gpu_helpers import codes_to_i8_layout
     g = torch.Generator().manual_seed(m * 7 + n + k)
     qa = torch.randint(-8, 8, (m, k), generator=g, dtype=torch.int8)
@@ -156,7 +156,7 @@ def test_i8_activation_gemm_exact(cuda_device, m, n, k, grouped, path):
     for fp32 in (False, True):
         out = Guarded((m, n), torch.float32 if fp32 else torch.bfloat16, d, -1234.0, float("nan"))
         wk.w4a4_grouped_gemm_i8(a8, pack(qw).to(d), sa.to(d), sw.to(d), out=out.view, out_fp32=fp32,
-                                force_stream=path == "mma_sync", tc_decode=path == "tc_decode")
+                                force_stream=path == "mma_sync")
         torch.cuda.synchronize()
         assert out.intact()
         ref = oracle_out(qa, qw, sa, sw)
@@ -167,8 +167,7 @@ def test_i8_activation_gemm_exact(cuda_device, m, n, k, grouped, path):
     assert _native.device_error() == 0
 
 
-@pytest.mark.parametrize("tc_decode", [False, True], ids=["mma_sync", "tc_decode"])
-def test_i8_gemm_extreme_scales_use_exact_path(cuda_device, tc_decode):
+def test_i8_gemm_extreme_scales_use_exact_path(cuda_device):
     """Scales outside the two-FMA fast range take the reference's three-step form."""
     from gpu_helpers import codes_to_i8_layout
     m, n, k = 16, 64, 1024
@@ -182,5 +181,5 @@ def test_i8_gemm_extreme_scales_use_exact_path(cuda_device, tc_decode):
     sw[3, 2] = 2.0 ** -120
     d = cuda_device
     got = wk.w4a4_grouped_gemm_i8(codes_to_i8_layout(qa).to(d), pack(qw).to(d), sa.to(d), sw.to(d),
-                                  out_fp32=True, tc_decode=tc_decode).cpu().numpy()
+                                  out_fp32=True).cpu().numpy()
     np.testing.assert_array_equal(got, oracle_out(qa, qw, sa, sw))
