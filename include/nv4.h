@@ -231,6 +231,25 @@ int nv4_w4a4_gemm_peer_allreduce_bf16(const void* a_codes, const void* w_packed,
                                       const void* w_scale, void* out, int64_t m, int64_t n, int64_t k, int flags,
                                       void* const* bufs, int rank, int world, int64_t capacity, void* stream);
 
+/*
+ * Launch plan of the decode (weight-streaming) GEMM that nv4_w4a4_gemm_i8 /
+ * nv4_w4a4_grouped_gemm use for m <= 64 tokens, computed on the host only
+ * (no GPU or CUDA call; sm_count is 148 on B200).  No reference counterpart:
+ * the reference's TileLang configs (nanovllm/kernels/w4a4_grouped_kernel.py:
+ * 21-28, 94-101) pick tile sizes from a JSON table instead.  peer != 0 plans
+ * the fused row-parallel form (nv4_w4a4_gemm_peer_allreduce_bf16), whose grid
+ * is limited to NV4_PEER_MAX_CTAS CTAs.  plan receives NV4_STREAM_PLAN_FIELDS
+ * int32 values, in order: token tiles (8 tokens each) per CTA, 16-row weight
+ * slabs per CTA, K-split warps per slab, token splits, token tiles per warp,
+ * weight rows per CTA, ring stages, K stages (two groups each), shared memory
+ * bytes, grid x, grid y, threads per CTA, producer warps.  The ring holds at
+ * least min(K stages, K-split warps + producer warps) stages.  Returns NV4_OK,
+ * or NV4_ERR_UNSUPPORTED for a shape the kernel cannot plan.
+ */
+#define NV4_STREAM_PLAN_FIELDS 13
+#define NV4_PEER_MAX_CTAS 256
+int nv4_w4a4_stream_plan(int64_t m, int64_t n, int64_t k, int flags, int sm_count, int peer, int32_t* plan);
+
 /* Library metadata and error reporting. */
 int nv4_version(void);                      /* major*10000 + minor*100 + patch */
 const char* nv4_status_string(int status);  /* static string for a status code */

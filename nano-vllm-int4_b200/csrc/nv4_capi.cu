@@ -131,6 +131,18 @@ extern "C" {
 
 int nv4_version(void) { return 100; }  // 0.1.0
 
+int nv4_w4a4_stream_plan(int64_t m, int64_t n, int64_t k, int flags, int sm_count, int peer, int32_t* plan) {
+  if (plan == nullptr) return NV4_ERR_INVALID_ARGUMENT;
+  StreamPlan pl;
+  const int rc = plan_w4a4_stream(m, n, k, (flags & NV4_GEMM_W_SCALE_GROUPED) != 0, sm_count, peer != 0, &pl);
+  if (rc != NV4_OK) return rc;
+  const int32_t v[NV4_STREAM_PLAN_FIELDS] = {pl.token_tiles, pl.slabs, pl.k_split, pl.token_splits, pl.tiles_per_warp,
+                                             pl.rows_per_cta, pl.stages, pl.n_iters, pl.smem_bytes, pl.grid_x,
+                                             pl.grid_y, pl.threads, pl.producer_warps};
+  for (int i = 0; i < NV4_STREAM_PLAN_FIELDS; ++i) plan[i] = v[i];
+  return NV4_OK;
+}
+
 const char* nv4_status_string(int status) {
   switch (status) {
     case NV4_OK: return "ok";

@@ -79,6 +79,25 @@ int launch_w4a16_gemm_static(const void* x, const void* qweight, const void* qze
 bool w4a16_static_fits(int64_t m, int64_t n);  // (m, n) within the static scratch
 // Peer mode of the stream GEMM (row-parallel layers): the launcher fills in the
 // tile geometry the matching tile reduce needs.
+// Launch plan of the decode stream GEMM (w4a4_gemm.cu); the C ABI exports it
+// as nv4_w4a4_stream_plan for tests and tools.
+struct StreamPlan {
+  int token_tiles;     // 8-token tiles per CTA (1, 2 or 4)
+  int slabs;           // 16-row weight slabs per CTA
+  int k_split;         // consumer warps splitting K per slab (1 or 4)
+  int token_splits;    // consumer warp groups splitting the token tiles
+  int tiles_per_warp;  // token tiles per consumer warp
+  int rows_per_cta;    // 16 * slabs
+  int stages;          // shared-memory ring stages
+  int n_iters;         // stages of K (two 128-groups each)
+  int ds_bytes;        // K-split partial buffers
+  int smem_bytes;      // dynamic shared memory per CTA
+  int grid_x, grid_y;  // CTAs along N and along the token blocks
+  int threads;         // threads per CTA (producers + consumers)
+  int producer_warps;  // TMA-issuing warps, which take the stages round-robin
+};
+int plan_w4a4_stream(int64_t m, int64_t n, int64_t k, bool w_scale_grouped, int sms, bool peer, StreamPlan* out);
+
 struct PeerTarget {
   void* const* bufs;  // world peer buffers, this rank's at [rank]
   int rank, world;

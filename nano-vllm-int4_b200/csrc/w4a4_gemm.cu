@@ -711,15 +711,10 @@ static bool make_map_u16(CUtensorMap* map, const void* base, uint64_t rows, uint
                             CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
-// a8 != nullptr: activations in the widened INT8 layout [m, k]; else a_packed [m, k/2].
-int launch_w4a4_stream_gemm(const void* a_packed, const void* a8, const void* w_packed, const void* a_scale,
-                            const void* w_scale, void* out, int64_t m, int64_t n, int64_t k, int flags,
-                            cudaStream_t stream, PeerTarget* peer) {
-  const int sms = device_sm_count();
-  if (sms <= 0) return NV4_ERR_CUDA;
-  const bool wg = (flags & NV4_GEMM_W_SCALE_GROUPED) != 0;
-  const bool f32 = peer != nullptr || (flags & NV4_GEMM_OUT_FP32) != 0;
-  const bool use_a8 = a8 != nullptr;
+// Launch plan of the stream kernel: a pure function of the shape, the flags
+// and the SM count (no device calls), so the CPU tests can sweep it.
+int plan_w4a4_stream(int64_t m, int64_t n, int64_t k, bool wg, int sms, bool peer, StreamPlan* out) {
+  if (m < 1 || n < 1 || k < 128 || k % 128 || sms < 1 || out == nullptr) return NV4_ERR_INVALID_ARGUMENT;
   const int MT = m <= 8 ? 1 : (m <= 16 ? 2 : 4);
   const int MP = MT * 8;
   const int64_t mblocks = (m + MP - 1) / MP;
@@ -742,8 +737,10 @@ int launch_w4a4_stream_gemm(const void* a_packed, const void* a8, const void* w_
   // with fewer, a producer can pass the wait one phase early and a TMA copy
   // can overwrite a slot still being read.  Fewer slabs per CTA until it fits.
   if (slabs > 4 && slabs <= 8) slabs = 4;
+  // Peer mode stores one flag per CTA, so the grid must fit kPeerSlots: start
+  // from enough slabs per CTA for that (the ring rule may still lower it).
+  if (peer) slabs = std::max<int>(slabs, static_cast<int>(std::min<int64_t>(kMaxWideSlabs, (total_slabs + kPeerSlots - 1) / kPeerSlots)));
   const int n_iters = (G + 1) / 2;
-  const bool scale_tma = (G % 8) == 0 && (reinterpret_cast<uintptr_t>(w_scale) & 15) == 0;
   int ks = 0, ts = 1, tpw = MT, ds_bytes = 0, R = 0, stages = 0;
   for (;;) {
     ks = slabs <= 4 ? 4 : 1;
@@ -762,7 +759,44 @@ int launch_w4a4_stream_gemm(const void* a_packed, const void* a8, const void* w_
   }
   if (stages < 1 || stages < std::min(n_iters, ks + kProducerWarps)) return NV4_ERR_UNSUPPORTED;
   const StreamLayout lay(R, MP, G, stages, wg, ds_bytes);
-  const int smem = lay.total + 1024;
+  StreamPlan pl;
+  pl.token_tiles = MT;
+  pl.slabs = slabs;
+  pl.k_split = ks;
+  pl.token_splits = ts;
+  pl.tiles_per_warp = tpw;
+  pl.rows_per_cta = R;
+  pl.stages = stages;
+  pl.n_iters = n_iters;
+  pl.ds_bytes = ds_bytes;
+  pl.smem_bytes = lay.total + 1024;
+  pl.grid_x = static_cast<int>((n + R - 1) / R);
+  pl.grid_y = static_cast<int>(mblocks);
+  pl.threads = 32 * (kProducerWarps + slabs * ts * ks);
+  pl.producer_warps = kProducerWarps;
+  if (pl.smem_bytes > kSmemLimit) return NV4_ERR_UNSUPPORTED;
+  if (peer && (mblocks != 1 || pl.grid_x > kPeerSlots)) return NV4_ERR_UNSUPPORTED;
+  *out = pl;
+  return NV4_OK;
+}
+
+// a8 != nullptr: activations in the widened INT8 layout [m, k]; else a_packed [m, k/2].
+int launch_w4a4_stream_gemm(const void* a_packed, const void* a8, const void* w_packed, const void* a_scale,
+                            const void* w_scale, void* out, int64_t m, int64_t n, int64_t k, int flags,
+                            cudaStream_t stream, PeerTarget* peer) {
+  const int sms = device_sm_count();
+  if (sms <= 0) return NV4_ERR_CUDA;
+  const bool wg = (flags & NV4_GEMM_W_SCALE_GROUPED) != 0;
+  const bool f32 = peer != nullptr || (flags & NV4_GEMM_OUT_FP32) != 0;
+  const bool use_a8 = a8 != nullptr;
+  if (peer && (peer->world < 2 || peer->world > kPeerMaxRanks)) return NV4_ERR_UNSUPPORTED;
+  StreamPlan pl;
+  const int prc = plan_w4a4_stream(m, n, k, wg, sms, peer != nullptr, &pl);
+  if (prc != NV4_OK) return prc;
+  const int MT = pl.token_tiles, MP = MT * 8, G = static_cast<int>(k / 128);
+  const int R = pl.rows_per_cta, stages = pl.stages, slabs = pl.slabs, ks = pl.k_split, tpw = pl.tiles_per_warp;
+  const int smem = pl.smem_bytes;
+  const bool scale_tma = (G % 8) == 0 && (reinterpret_cast<uintptr_t>(w_scale) & 15) == 0;
 
   CUtensorMap maps[3];
   memset(maps, 0, sizeof(maps));
@@ -790,17 +824,15 @@ int launch_w4a4_stream_gemm(const void* a_packed, const void* a8, const void* w_
   a.G = G;
   a.R = R;
   a.slabs = slabs;
-  a.n_iters = n_iters;
+  a.n_iters = pl.n_iters;
   a.stages = stages;
   a.scale_tma = scale_tma ? 1 : 0;
-  const dim3 grid(static_cast<unsigned>((n + R - 1) / R), static_cast<unsigned>(mblocks));
+  const dim3 grid(static_cast<unsigned>(pl.grid_x), static_cast<unsigned>(pl.grid_y));
   for (int r = 0; r < kPeerMaxRanks; ++r) a.peer_bufs[r] = nullptr;
   a.peer_capacity = 0;
   a.peer_rank = 0;
   a.peer_world = 0;
   if (peer) {
-    if (mblocks != 1 || grid.x > static_cast<unsigned>(kPeerSlots) || peer->world < 2 || peer->world > kPeerMaxRanks)
-      return NV4_ERR_UNSUPPORTED;
     for (int r = 0; r < peer->world; ++r) a.peer_bufs[r] = static_cast<uint8_t*>(peer->bufs[r]);
     a.peer_capacity = peer->capacity;
     a.peer_rank = peer->rank;
@@ -808,7 +840,7 @@ int launch_w4a4_stream_gemm(const void* a_packed, const void* a8, const void* w_
     peer->rows_per_cta = R;
     peer->ctas = static_cast<int>(grid.x);
   }
-  const int threads = 32 * (kProducerWarps + slabs * ts * ks);
+  const int threads = pl.threads;
   switch (MT * 100 + tpw * 10 + ks) {
     case 111: return launch_flags<1, 1, 1>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);
     case 114: return launch_flags<1, 1, 4>(maps, a, grid, threads, smem, use_a8, wg, f32, stream);

@@ -37,7 +37,7 @@ EXPORTS = ("nv4_rht_quant_pack", "nv4_rht_quant_i8", "nv4_w4a4_grouped_gemm", "n
            "nv4_device_error", "nv4_w4a16_gemm_static", "nv4_peer_header_bytes", "nv4_peer_buffer_alloc",
            "nv4_peer_buffer_open", "nv4_peer_buffer_close", "nv4_peer_buffer_free", "nv4_peer_allreduce_bf16",
            "nv4_w4a4_gemm_peer_allreduce_bf16", "nv4_silu_mul_rht_quant_i8",
-           "nv4_add_rmsnorm_rht_quant_i8")
+           "nv4_add_rmsnorm_rht_quant_i8", "nv4_w4a4_stream_plan")
 
 
 class NativeLibraryError(RuntimeError):
@@ -119,6 +119,8 @@ def load(path: str | None = None) -> ctypes.CDLL:
                      "nv4_peer_allreduce_bf16", "nv4_w4a4_gemm_peer_allreduce_bf16"):
             getattr(lib, name).restype = _int
         lib.nv4_w4a16_workspace_bytes.restype = _i64
+        lib.nv4_w4a4_stream_plan.argtypes = [_i64, _i64, _i64, _int, _int, _int, ctypes.POINTER(ctypes.c_int32)]
+        lib.nv4_w4a4_stream_plan.restype = _int
         lib.nv4_status_string.argtypes = [_int]
         lib.nv4_status_string.restype = ctypes.c_char_p
         lib.nv4_device_error.argtypes = [ctypes.POINTER(_int)]
@@ -245,6 +247,24 @@ def w4a16_gemm_static(x, qweight, qzeros, scales, out, group_size: int) -> None:
             raise ValueError(f"nv4_w4a16_gemm_static: m * n = {m * n} exceeds the static scratch of "
                              f"{W4A16_STATIC_SCRATCH_FLOATS} floats (m <= 16); use nv4_w4a16_gemm with a workspace")
         check(status, "nv4_w4a16_gemm_static")
+
+
+STREAM_PLAN_FIELDS = ("token_tiles", "slabs", "k_split", "token_splits", "tiles_per_warp", "rows_per_cta", "stages",
+                      "n_iters", "smem_bytes", "grid_x", "grid_y", "threads", "producer_warps")
+SM_COUNT_B200 = 148
+
+
+def w4a4_stream_plan(m: int, n: int, k: int, flags: int = GEMM_W_SCALE_GROUPED, sm_count: int = SM_COUNT_B200,
+                     peer: bool = False):
+    """Host-side launch plan of the decode stream GEMM (nv4_w4a4_stream_plan;
+    no GPU needed): a dict of STREAM_PLAN_FIELDS, or None when the kernel
+    cannot plan the shape (NV4_ERR_UNSUPPORTED)."""
+    out = (ctypes.c_int32 * len(STREAM_PLAN_FIELDS))()
+    status = load().nv4_w4a4_stream_plan(m, n, k, flags, sm_count, 1 if peer else 0, out)
+    if status == ERR_UNSUPPORTED:
+        return None
+    check(status, "nv4_w4a4_stream_plan")
+    return dict(zip(STREAM_PLAN_FIELDS, list(out)))
 
 
 # ---------------------------------------------------------------- tensor-parallel peer buffers

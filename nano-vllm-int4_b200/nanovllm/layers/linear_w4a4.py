@@ -314,6 +314,20 @@ class W4A4RowParallelLinear(W4A4Linear):
         self.register_buffer("signs", torch.empty(input_size if self.gather_input else k_local, dtype=torch.int8))
         self.use_peer_allreduce = True
         self.fuse_peer_gemm = True
+        self._fused_peer_ok = {}  # tokens -> whether the fused peer GEMM can plan this shape
+
+    def _fused_peer_plannable(self, m: int, device) -> bool:
+        """Whether the fused peer-memory GEMM has a launch plan for m tokens (its
+        grid must fit the per-CTA flag slots).  The plan depends only on the
+        shape and the SM count, so every rank of the group decides alike and
+        falls back to the same path."""
+        ok = self._fused_peer_ok.get(m)
+        if ok is None:
+            sms = torch.cuda.get_device_properties(device).multi_processor_count
+            ok = _native.w4a4_stream_plan(m, self.out_features, self.in_features, _native.GEMM_W_SCALE_GROUPED,
+                                          sm_count=sms, peer=True) is not None
+            self._fused_peer_ok[m] = ok
+        return ok
 
     def _peer_buffers(self, device):
         """The group's peer buffers, setting them up on first use (collective)."""
@@ -364,7 +378,7 @@ class W4A4RowParallelLinear(W4A4Linear):
             m = codes.shape[0]
             count = m * self.out_features
             peers = self._peer_buffers(codes.device) if m <= self.PEER_MAX_TOKENS else None
-            if peers and count <= PEER_CAPACITY and self.fuse_peer_gemm:
+            if peers and count <= PEER_CAPACITY and self.fuse_peer_gemm and self._fused_peer_plannable(m, codes.device):
                 out = torch.empty((m, self.out_features), dtype=torch.bfloat16, device=codes.device)
                 _native.w4a4_gemm_peer_allreduce_bf16(codes, self.packed_weight, scale, self.weight_scale, out, peers,
                                                       self.tp_rank, PEER_CAPACITY, _native.GEMM_W_SCALE_GROUPED)
