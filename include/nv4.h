@@ -250,6 +250,49 @@ int nv4_w4a4_gemm_peer_allreduce_bf16(const void* a_codes, const void* w_packed,
 #define NV4_PEER_MAX_CTAS 256
 int nv4_w4a4_stream_plan(int64_t m, int64_t n, int64_t k, int flags, int sm_count, int peer, int32_t* plan);
 
+/*
+ * Decode attention over the paged BF16 KV cache of the end-to-end model:
+ * replaces flash_attn_with_kvcache in nanovllm/layers/attention.py:71-73
+ * (causal, one query token per sequence).
+ *
+ *   q             bf16 [batch, num_heads, head_dim] (the current token's queries)
+ *   k_cache/v_cache  bf16 [pages, page_size, num_kv_heads, head_dim]
+ *   block_tables  int32 [batch, max_pages]: page of each 256-token block
+ *   context_lens  int32 [batch]: tokens of each sequence (including the current
+ *                 one); 0 marks a padding row, whose output is zero
+ *   out           bf16 [batch, num_heads, head_dim]
+ *   workspace     nv4_paged_attention_workspace_bytes(batch, num_heads, max_pages) bytes
+ * Query head h attends with KV head h / (num_heads / num_kv_heads) (grouped-
+ * query attention, at most 8 query heads per KV head); softmax scale `scale`.
+ * Requirements: head_dim == 128, page_size == 256.
+ */
+int64_t nv4_paged_attention_workspace_bytes(int64_t batch, int64_t num_heads, int64_t max_pages);
+int nv4_paged_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int32_t* block_tables,
+                               const int32_t* context_lens, void* out, void* workspace, int64_t workspace_bytes,
+                               int64_t batch, int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+                               int64_t page_size, int64_t max_pages, float scale, void* stream);
+
+/*
+ * Per-head q/k RMSNorm, rotary embedding and KV-cache store of the fused QKV
+ * projection output, one kernel (nanovllm/models/qwen3.py:87-92 q_norm /
+ * k_norm / rotary_emb, and nanovllm/layers/attention.py:10-40 store_kvcache):
+ *
+ *   qkv        bf16 [tokens, (num_heads + 2 * num_kv_heads) * head_dim]: q | k | v
+ *   q_weight, k_weight  bf16 [head_dim] RMSNorm weights; eps as the model's
+ *   cos_sin    float32 [max_position, head_dim]: cos in the first half, sin in the second
+ *   positions  int64 [tokens]
+ *   slot_mapping int32 [tokens]: cache row (page * page_size + offset); < 0 stores nothing
+ *   q_out      bf16 [tokens, num_heads, head_dim]
+ *   k_out      bf16 [tokens, num_kv_heads, head_dim] or NULL (prefill attention input)
+ *   k_cache/v_cache as nv4_paged_decode_attention (NULL with slot_mapping NULL: no store)
+ * RMSNorm bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w); rotary on FP32 copies,
+ * y1 = x1 cos - x2 sin, y2 = x2 cos + x1 sin, rounded to BF16.  head_dim == 128.
+ */
+int nv4_qk_norm_rope_store(const void* qkv, const void* q_weight, const void* k_weight, const float* cos_sin,
+                           const int64_t* positions, const int32_t* slot_mapping, void* q_out, void* k_out,
+                           void* k_cache, void* v_cache, int64_t tokens, int64_t num_heads, int64_t num_kv_heads,
+                           int64_t head_dim, float eps, void* stream);
+
 /* Library metadata and error reporting. */
 int nv4_version(void);                      /* major*10000 + minor*100 + patch */
 const char* nv4_status_string(int status);  /* static string for a status code */

@@ -394,5 +394,49 @@ int nv4_w4a4_gemm_peer_allreduce_bf16(const void* a_codes, const void* w_packed,
                                        peer.rows_per_cta, peer.ctas, capacity, s);
 }
 
+// ---- attention of the end-to-end model
+int64_t nv4_paged_attention_workspace_bytes(int64_t batch, int64_t num_heads, int64_t max_pages) {
+  if (batch < 1 || num_heads < 1 || max_pages < 1) return 0;
+  return paged_attention_workspace_bytes(batch, num_heads, max_pages);
+}
+
+int nv4_paged_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int32_t* block_tables,
+                               const int32_t* context_lens, void* out, void* workspace, int64_t workspace_bytes,
+                               int64_t batch, int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+                               int64_t page_size, int64_t max_pages, float scale, void* stream) {
+  if (!q || !k_cache || !v_cache || !block_tables || !context_lens || !out || !workspace)
+    return NV4_ERR_INVALID_ARGUMENT;
+  if (batch < 1 || batch > 65535 || num_kv_heads < 1 || num_heads < num_kv_heads || num_heads % num_kv_heads ||
+      max_pages < 1 || max_pages > 65535 || !(scale > 0.0f))
+    return NV4_ERR_INVALID_ARGUMENT;
+  if (head_dim != 128 || page_size != 256 || num_heads / num_kv_heads > 8) return NV4_ERR_UNSUPPORTED;
+  if (workspace_bytes < paged_attention_workspace_bytes(batch, num_heads, max_pages)) return NV4_ERR_INVALID_ARGUMENT;
+  if (!aligned(q, 16) || !aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(out, 4) ||
+      !aligned(workspace, 16) || !aligned(block_tables, 4) || !aligned(context_lens, 4))
+    return NV4_ERR_ALIGNMENT;
+  if (!device_is_sm100()) return NV4_ERR_DEVICE;
+  return launch_paged_decode_attention(q, k_cache, v_cache, block_tables, context_lens, out, workspace, batch,
+                                       num_heads, num_kv_heads, max_pages, scale, static_cast<cudaStream_t>(stream));
+}
+
+int nv4_qk_norm_rope_store(const void* qkv, const void* q_weight, const void* k_weight, const float* cos_sin,
+                           const int64_t* positions, const int32_t* slot_mapping, void* q_out, void* k_out,
+                           void* k_cache, void* v_cache, int64_t tokens, int64_t num_heads, int64_t num_kv_heads,
+                           int64_t head_dim, float eps, void* stream) {
+  if (!qkv || !q_weight || !k_weight || !cos_sin || !positions || !q_out) return NV4_ERR_INVALID_ARGUMENT;
+  if ((slot_mapping != nullptr) != (k_cache != nullptr) || (k_cache != nullptr) != (v_cache != nullptr))
+    return NV4_ERR_INVALID_ARGUMENT;
+  if (tokens < 1 || num_heads < 1 || num_kv_heads < 1 || tokens * (num_heads + 2 * num_kv_heads) > (int64_t(1) << 31))
+    return NV4_ERR_INVALID_ARGUMENT;
+  if (head_dim != 128) return NV4_ERR_UNSUPPORTED;
+  if (!aligned(qkv, 8) || !aligned(q_weight, 8) || !aligned(k_weight, 8) || !aligned(cos_sin, 4) ||
+      !aligned(q_out, 8) || (k_out && !aligned(k_out, 8)) || (k_cache && !aligned(k_cache, 8)) ||
+      (v_cache && !aligned(v_cache, 8)))
+    return NV4_ERR_ALIGNMENT;
+  if (!device_is_sm100()) return NV4_ERR_DEVICE;
+  return launch_qk_norm_rope_store(qkv, q_weight, k_weight, cos_sin, positions, slot_mapping, q_out, k_out, k_cache,
+                                   v_cache, tokens, num_heads, num_kv_heads, eps, static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"
 #pragma GCC visibility pop

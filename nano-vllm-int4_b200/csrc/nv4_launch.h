@@ -77,6 +77,16 @@ int64_t w4a16_workspace_bytes(int64_t m, int64_t n, int64_t k);
 int launch_w4a16_gemm_static(const void* x, const void* qweight, const void* qzeros, const void* scales, void* out,
                              int64_t m, int64_t n, int64_t k, cudaStream_t stream);
 bool w4a16_static_fits(int64_t m, int64_t n);  // (m, n) within the static scratch
+// Paged decode attention and the q/k norm + rotary + KV store (attention.cu).
+int64_t paged_attention_workspace_bytes(int64_t batch, int64_t num_heads, int64_t max_pages);
+int launch_paged_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int* block_tables,
+                                  const int* context_lens, void* out, void* workspace, int64_t batch,
+                                  int64_t num_heads, int64_t num_kv_heads, int64_t max_pages, float scale,
+                                  cudaStream_t stream);
+int launch_qk_norm_rope_store(const void* qkv, const void* q_weight, const void* k_weight, const float* cos_sin,
+                              const int64_t* positions, const int* slot_mapping, void* q_out, void* k_out,
+                              void* k_cache, void* v_cache, int64_t tokens, int64_t num_heads, int64_t num_kv_heads,
+                              float eps, cudaStream_t stream);
 // Peer mode of the stream GEMM (row-parallel layers): the launcher fills in the
 // tile geometry the matching tile reduce needs.
 // Launch plan of the decode stream GEMM (w4a4_gemm.cu); the C ABI exports it

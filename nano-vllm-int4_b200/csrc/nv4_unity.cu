@@ -5,3 +5,4 @@
 #include "w4a4_gemm_tc.cu"
 #include "w4a16_gemm.cu"
 #include "peer_allreduce.cu"
+#include "attention.cu"

@@ -37,7 +37,8 @@ EXPORTS = ("nv4_rht_quant_pack", "nv4_rht_quant_i8", "nv4_w4a4_grouped_gemm", "n
            "nv4_device_error", "nv4_w4a16_gemm_static", "nv4_peer_header_bytes", "nv4_peer_buffer_alloc",
            "nv4_peer_buffer_open", "nv4_peer_buffer_close", "nv4_peer_buffer_free", "nv4_peer_allreduce_bf16",
            "nv4_w4a4_gemm_peer_allreduce_bf16", "nv4_silu_mul_rht_quant_i8",
-           "nv4_add_rmsnorm_rht_quant_i8", "nv4_w4a4_stream_plan")
+           "nv4_add_rmsnorm_rht_quant_i8", "nv4_w4a4_stream_plan", "nv4_paged_attention_workspace_bytes",
+           "nv4_paged_decode_attention", "nv4_qk_norm_rope_store")
 
 
 class NativeLibraryError(RuntimeError):
@@ -121,6 +122,14 @@ def load(path: str | None = None) -> ctypes.CDLL:
         lib.nv4_w4a16_workspace_bytes.restype = _i64
         lib.nv4_w4a4_stream_plan.argtypes = [_i64, _i64, _i64, _int, _int, _int, ctypes.POINTER(ctypes.c_int32)]
         lib.nv4_w4a4_stream_plan.restype = _int
+        lib.nv4_paged_attention_workspace_bytes.argtypes = [_i64, _i64, _i64]
+        lib.nv4_paged_attention_workspace_bytes.restype = _i64
+        lib.nv4_paged_decode_attention.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
+                                                   _i64, _i64, ctypes.c_float, _vp]
+        lib.nv4_paged_decode_attention.restype = _int
+        lib.nv4_qk_norm_rope_store.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64,
+                                               _i64, ctypes.c_float, _vp]
+        lib.nv4_qk_norm_rope_store.restype = _int
         lib.nv4_status_string.argtypes = [_int]
         lib.nv4_status_string.restype = ctypes.c_char_p
         lib.nv4_device_error.argtypes = [ctypes.POINTER(_int)]
@@ -329,3 +338,34 @@ def peer_allreduce_bf16(bufs: list[int], rank: int, out, count: int, capacity: i
     with torch.cuda.device(out.device):
         check(load().nv4_peer_allreduce_bf16(arr, rank, len(bufs), ptr(out), count, capacity, stream_of(out)),
               "nv4_peer_allreduce_bf16")
+
+
+# ---------------------------------------------------------------- attention of the end-to-end model
+def paged_attention_workspace_bytes(batch: int, num_heads: int, max_pages: int) -> int:
+    return int(load().nv4_paged_attention_workspace_bytes(batch, num_heads, max_pages))
+
+
+def paged_decode_attention(q, k_cache, v_cache, block_tables, context_lens, out, workspace, scale: float) -> None:
+    """nv4_paged_decode_attention: q [B, Hq, D], caches [pages, 256, Hkv, D],
+    block_tables int32 [B, max_pages], context_lens int32 [B] -> out [B, Hq, D]."""
+    b, hq, d = q.shape
+    hkv = k_cache.shape[2]
+    with torch.cuda.device(q.device):
+        check(load().nv4_paged_decode_attention(ptr(q), ptr(k_cache), ptr(v_cache), ptr(block_tables),
+                                                ptr(context_lens), ptr(out), ptr(workspace),
+                                                workspace.numel() * workspace.element_size(), b, hq, hkv, d,
+                                                k_cache.shape[1], block_tables.shape[1], float(scale), stream_of(q)),
+              "nv4_paged_decode_attention")
+
+
+def qk_norm_rope_store(qkv, q_weight, k_weight, cos_sin, positions, slot_mapping, q_out, k_out, k_cache, v_cache,
+                       num_heads: int, num_kv_heads: int, eps: float) -> None:
+    """nv4_qk_norm_rope_store (k_out, and slot_mapping with both caches, may be None)."""
+    t = qkv.shape[0]
+    nul = ctypes.c_void_p(0)
+    opt = lambda x: nul if x is None else ptr(x)
+    with torch.cuda.device(qkv.device):
+        check(load().nv4_qk_norm_rope_store(ptr(qkv), ptr(q_weight), ptr(k_weight), ptr(cos_sin), ptr(positions),
+                                            opt(slot_mapping), ptr(q_out), opt(k_out), opt(k_cache), opt(v_cache), t,
+                                            num_heads, num_kv_heads, q_out.shape[-1], float(eps), stream_of(qkv)),
+              "nv4_qk_norm_rope_store")

@@ -82,6 +82,15 @@ def validate_manifest(manifest: dict) -> dict:
     return declared
 
 
+def checkpoint_activation_contract(checkpoint_path) -> tuple[str, int]:
+    """(activation layout, lowest code) the checkpoint's modules must be built
+    with: the format fixes the full-width row_DH transform and codes in [-7, 7]
+    (nanovllm/layers/linear_w4a4.py:23-36 of the reference)."""
+    manifest = json.loads((Path(checkpoint_path) / "manifest.json").read_text())
+    validate_manifest(manifest)
+    return LAYOUT, -7
+
+
 @dataclass(frozen=True)
 class ShardPlan:
     """What one rank keeps of a fused projection: per source matrix a row range

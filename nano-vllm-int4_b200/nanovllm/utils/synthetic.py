@@ -122,3 +122,26 @@ def w4a16_weights(n: int, k: int, seed: int, group: int = GROUP):
     qzeros = (z.reshape(k // group, n // 8, 8) << shifts[None, None, :]).sum(2)
     to_i32 = lambda t: torch.where(t >= 2 ** 31, t - 2 ** 32, t).to(torch.int32).contiguous()
     return to_i32(qweight), to_i32(qzeros), scales.contiguous()
+
+
+# Qwen3-8B architecture (the benchmark's end-to-end configuration): no weights
+# exist offline, so the engine runs it with load_format="dummy".
+QWEN3_8B_CONFIG = {
+    "architectures": ["Qwen3ForCausalLM"], "model_type": "qwen3", "hidden_size": 4096,
+    "intermediate_size": 12288, "num_hidden_layers": 36, "num_attention_heads": 32, "num_key_value_heads": 8,
+    "head_dim": 128, "hidden_act": "silu", "rms_norm_eps": 1e-6, "rope_theta": 1000000.0,
+    "max_position_embeddings": 40960, "vocab_size": 151936, "tie_word_embeddings": False,
+    "attention_bias": False, "torch_dtype": "bfloat16", "bos_token_id": 151643, "eos_token_id": 151645,
+}
+
+
+def write_qwen3_config(directory: str, **overrides) -> str:
+    """Write a Hugging Face config.json for a Qwen3 model (Qwen3-8B unless
+    overridden, e.g. fewer layers for tests) into `directory`; returns it."""
+    import json
+    import os
+    os.makedirs(directory, exist_ok=True)
+    cfg = dict(QWEN3_8B_CONFIG, **overrides)
+    with open(os.path.join(directory, "config.json"), "w") as f:
+        json.dump(cfg, f, indent=1)
+    return directory
