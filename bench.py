@@ -24,6 +24,11 @@ replayed, as the reference's model runner does for decode.
   * ``--mode dp``: N independent replicas, each with its own batch of 32 (weak
     scaling); ``value`` is all ranks' bytes over the slowest rank's time.
 
+Every run (1 GPU, and TP at N > 1) also carries ``model_decode``: BASELINE
+config 4, a random-init Qwen3-8B through the engine's public API (32 requests
+of 4096 tokens, then 256 batch-32 greedy decode steps, CUDA graphs), with W4A4
+and with BF16 cuBLAS linears: decode tokens/s of both and their ratio.
+
 At one GPU the line also carries ``configs``: every configuration BASELINE
 names, measured in the same run -- config 1 per projection at M in {1, 8, 32}
 (GEMM launches over 36 distinct weight sets, and the prep launch), config 2
@@ -520,6 +525,47 @@ def measure_bf16_chain(device, stream, layers, x_dev):
             "api": "torch.nn.functional.linear (cuBLAS) BF16, same chain and producers, CUDA graph"}
 
 
+# ---------------------------------------------------------------- config 4: the end-to-end model
+E2E_REQUESTS, E2E_PROMPT, E2E_DECODE = 32, 4096, 256
+
+
+def measure_model(world: int, prompt_len: int = E2E_PROMPT, decode: int = E2E_DECODE):
+    """Config 4: random-init Qwen3-8B through the engine's public API
+    (``LLM(..., w4a4_checkpoint=..., tensor_parallel_size=world)`` then
+    ``generate``): 32 requests of `prompt_len` uniform random token ids, serial
+    prefill, then batch-32 greedy decode for `decode` tokens, CUDA graphs on,
+    prefix reuse off; once with W4A4 linears and once with BF16 cuBLAS linears
+    (the same-box comparator).  Decode tok/s = decode tokens / decode wall time
+    (each step ends with the sampled token ids on the host)."""
+    import gc
+    import tempfile
+    from nanovllm import LLM, SamplingParams
+    model_dir = synthetic.write_qwen3_config(tempfile.mkdtemp(prefix="qwen3_8b_"))
+    g = torch.Generator().manual_seed(2026)
+    prompts = [torch.randint(0, synthetic.QWEN3_8B_CONFIG["vocab_size"], (prompt_len,), generator=g).tolist()
+               for _ in range(E2E_REQUESTS)]
+    params = SamplingParams(temperature=0.0, max_tokens=decode, ignore_eos=True)
+    out = {"requests": E2E_REQUESTS, "prompt_tokens": prompt_len, "decode_tokens": decode,
+           "model": "Qwen3-8B architecture, random init (36 layers, hidden 4096, 32/8 heads, vocab 151936)",
+           "api": "nanovllm.LLM(...).generate, greedy, CUDA graphs, prefix reuse off", "tp": world}
+    for arm, kw in (("w4a4", {"w4a4_checkpoint": "random"}), ("bf16", {})):
+        llm = LLM(model_dir, load_format="dummy", max_model_len=prompt_len + decode + 8,
+                  max_num_batched_tokens=16384, max_num_seqs=E2E_REQUESTS, tensor_parallel_size=world, **kw)
+        try:
+            llm.generate(prompts, params)
+            st = dict(llm.stats)
+        finally:
+            llm.exit()
+            del llm
+            gc.collect()
+            torch.cuda.empty_cache()
+        out[arm] = {"decode_tok_s": st["decode_tokens"] / st["decode_s"],
+                    "ms_per_decode_step": st["decode_s"] / st["decode_steps"] * 1e3,
+                    "prefill_tok_s": st["prefill_tokens"] / st["prefill_s"], **st}
+    out["decode_speedup_w4a4_vs_bf16"] = out["w4a4"]["decode_tok_s"] / out["bf16"]["decode_tok_s"]
+    return out
+
+
 # ---------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser(description=__doc__)
@@ -532,6 +578,7 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the per-config measurements (1 GPU)")
+    ap.add_argument("--no-model", action="store_true", help="skip the end-to-end model (config 4)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -668,6 +715,13 @@ def main():
         cfg["peaks"] = {"hbm_gbs": peaks["hbm_gbs"], "bf16_tflops": peaks["bf16_tflops"],
                         "bf16_tflops_sustained": peaks["bf16_tflops_sustained"], "kind": peak_kind}
         line["configs"] = cfg
+    if not args.no_model and mode != "dp":
+        mods = gu = outs = None  # the chain's weights are not needed any more
+        torch.cuda.empty_cache()
+        try:
+            line["model_decode"] = measure_model(world)
+        except Exception as e:  # the headline line still prints
+            line["model_decode"] = {"error": repr(e)[:300]}
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()

@@ -78,7 +78,7 @@ def pack_int4(codes: torch.Tensor) -> torch.Tensor:
 def grouped_gemm(qa: torch.Tensor, qw: torch.Tensor, sa: torch.Tensor, sw: torch.Tensor) -> torch.Tensor:
     """FP32 INT4 group dots, FP64 product and sum rounded to FP32 per group."""
     m, k = qa.shape
-    total = torch.zeros((m, qw.shape[0]), dtype=torch.float32)
+    total = torch.zeros((m, qw.shape[0]), dtype=torch.float32, device=qa.device)
     qaf, qwf = qa.float(), qw.float()
     for g in range(k // GROUP):
         sl = slice(g * GROUP, (g + 1) * GROUP)
@@ -93,7 +93,7 @@ def w4a4_linear(x: torch.Tensor, signs: torch.Tensor, w_codes: torch.Tensor, w_s
     """One W4A4 linear (block128 layout): x bf16 [M, K] -> bf16 [M, N]."""
     codes, scale = quantize_rotated(rotate_block128(x, signs), clamp_lo)
     pack_int4(codes)
-    return grouped_gemm(codes, w_codes, scale, w_scale).bfloat16()
+    return grouped_gemm(codes, w_codes.to(x.device), scale, w_scale.to(x.device)).bfloat16()
 
 
 def add_rmsnorm(x: torch.Tensor, residual, weight: torch.Tensor, eps: float):
