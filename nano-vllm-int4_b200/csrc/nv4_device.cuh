@@ -100,20 +100,32 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete is
+// suspended (it issues nothing) until the phase completes or the hint expires,
+// so waiting warps do not take issue slots from the warps doing the work.
+constexpr uint32_t kSuspendHintNs = 100000;  // 100 us per suspension
+
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait on an mbarrier phase.  Returns false (and records `err`) when
 // the phase did not complete within kWaitLimitNs or another CTA already
 // reported an error.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int err) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_timer_ns();
-  uint32_t spins = 0;
-  while (!mbar_try_wait(bar, parity)) {
-    if ((++spins & 255u) == 0) {
-      if (error_raised()) return false;
-      if (global_timer_ns() - start > kWaitLimitNs) {
-        record_error(err);
-        return false;
-      }
+  while (!mbar_try_wait_suspend(bar, parity)) {
+    if (error_raised()) return false;
+    if (global_timer_ns() - start > kWaitLimitNs) {
+      record_error(err);
+      return false;
     }
   }
   return true;

@@ -183,3 +183,54 @@ def test_i8_gemm_extreme_scales_use_exact_path(cuda_device):
     got = wk.w4a4_grouped_gemm_i8(codes_to_i8_layout(qa).to(d), pack(qw).to(d), sa.to(d), sw.to(d),
                                   out_fp32=True).cpu().numpy()
     np.testing.assert_array_equal(got, oracle_out(qa, qw, sa, sw))
+
+
+@pytest.mark.parametrize("m", [512, 2048, 4096])
+@pytest.mark.parametrize("n,k", [(6144, 4096), (4096, 4096), (24576, 4096), (4096, 12288)])
+def test_prefill_config2_shapes_sampled(cuda_device, m, n, k):
+    """BASELINE config 2 at its real shapes on the tcgen05 kernel (the default
+    dispatch above 64 tokens): the full GEMM runs on the GPU, and a seeded
+    sample of 16 token rows x 512 weight columns is checked bit for bit
+    against the oracle (rows and columns of the GEMM are independent)."""
+    from gpu_helpers import codes_to_i8_layout
+    d = cuda_device
+    g = torch.Generator(device=d).manual_seed(m + n + k)
+    qa = torch.randint(-8, 8, (m, k), generator=g, dtype=torch.int8, device=d)
+    wp = torch.randint(-128, 128, (n, k // 2), generator=g, dtype=torch.int8, device=d)
+    sa = (torch.rand(m, k // 128, generator=g, device=d) * 2 + 0.01).bfloat16()
+    sw = (torch.rand(n, k // 128, generator=g, device=d) * .03 + 1e-4).bfloat16()
+    out = Guarded((m, n), torch.bfloat16, d, -1234.0, float("nan"))
+    wk.w4a4_grouped_gemm_i8(codes_to_i8_layout(qa), wp, sa, sw, out=out.view)
+    torch.cuda.synchronize()
+    assert out.intact() and _native.device_error() == 0
+    gs = torch.Generator().manual_seed(m * n)
+    rows = torch.randperm(m, generator=gs)[:16].sort().values
+    cols = torch.randperm(n, generator=gs)[:512].sort().values
+    qw = synthetic.unpack_int4(wp[cols.to(d)].cpu())
+    ref = oracle_out(qa[rows.to(d)].cpu(), qw, sa[rows.to(d)].cpu(), sw[cols.to(d)].cpu())
+    got = out.view[rows.to(d)][:, cols.to(d)]
+    np.testing.assert_array_equal(u16(got), o.f32_to_bf16_bits(ref))
+    assert not torch.isnan(out.view.float()).any()  # every element written
+
+
+@pytest.mark.parametrize("grouped", [True, False])
+def test_tc_extreme_scales_take_exact_path(cuda_device, grouped):
+    """Above 64 tokens (the tcgen05 kernel): scale blocks with a scale outside
+    the two-FMA range use the reference's three-step form, others the fast one,
+    in one launch."""
+    from gpu_helpers import codes_to_i8_layout
+    m, n, k = 200, 384, 2048
+    g = torch.Generator().manual_seed(13)
+    qa = torch.randint(-8, 8, (m, k), generator=g, dtype=torch.int8)
+    qw = torch.randint(-8, 8, (n, k), generator=g, dtype=torch.int8)
+    sa = (torch.rand(m, k // 128, generator=g) * 2).bfloat16()
+    sa[7, 3] = 2.0 ** -110      # group 3: slow for the tile holding token 7
+    sa[150, 12] = 2.0 ** 100    # group 12: slow for the tile holding token 150
+    sw = ((torch.rand(n, k // 128, generator=g) if grouped else torch.rand(n, generator=g)) * .03).bfloat16()
+    if grouped:
+        sw[300, 9] = 2.0 ** -120
+    d = cuda_device
+    got = wk.w4a4_grouped_gemm_i8(codes_to_i8_layout(qa).to(d), pack(qw).to(d), sa.to(d), sw.to(d),
+                                  out_fp32=True).cpu().numpy()
+    np.testing.assert_array_equal(got, oracle_out(qa, qw, sa, sw))
+    assert _native.device_error() == 0
