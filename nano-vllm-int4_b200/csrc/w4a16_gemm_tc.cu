@@ -1,0 +1,371 @@
+// Kernel D2: GPTQ W4A16 dequant GEMM on 5th-generation tensor cores (tcgen05
+// kind::f16), for prefill-shape token counts (more than 32 tokens).
+//
+// out[m, n] = sum_k x[m, k] * Wdq[k, n] with the reference's dequantisation
+// (nanovllm/layers/linear_w4a16.py:45-55): Wdq = bf16((w - z - 1) * bf16(scale)),
+// computed as bf16(128 + w) - bf16(129 + z) (exact) times the BF16-rounded FP16
+// scale (one BF16 rounding).  FP32 accumulation over all of K in tensor memory,
+// one BF16 rounding of the result; no split-K.  (The reference adds BF16-rounded
+// split-K partials with BF16 atomics, so results agree within a tolerance.)
+//
+// The MMA computes D[n, t] = A[n, k] * B[t, k]^T with
+//   A = dequantised weights: M = 128 weight columns n, held in tensor memory
+//       (column n in TMEM lane n, two BF16 k per 32-bit column, K-major), so
+//       the widened weights never touch shared memory;
+//   B = activations: N = BN tokens, BF16 K-major with the 128-byte swizzle,
+//       exactly as TMA lands them.
+// Persistent: one CTA per SM walks tiles of 128 weight columns x BN tokens
+// over all of K, 64 K per pipeline chunk:
+//   warp 0      TMA producer: x tile [BN x 64 k] and the packed weight tile
+//               [8 rows of k/8 x 128 columns] per chunk into an S-slot ring.
+//   warp 1      TMEM allocation (all 512 columns) and the single MMA-issuing
+//               thread: 4 x tcgen05.mma kind::f16 (K = 16) per chunk.
+//   warps 2-5   dequantisation, one warp per TMEM lane quarter: thread = weight
+//               column; 8 packed words -> 32 BF16 pairs -> tcgen05.st into the
+//               chunk's A buffer.
+//   warps 6-21  epilogue, four per lane quarter (BN/4 tokens each): tcgen05.ld,
+//               hand the accumulator back, round to BF16, store out[t, n].
+// TMEM columns: accumulators [0, 256) (one of 256 tokens or two of 128), A
+// buffers [256, 512) (32 columns per chunk, up to 8).
+//
+// Every wait is bounded; on a timeout the roles stop, the MMA thread waits for
+// its issued MMAs and the TMEM is freed before the CTA exits.
+#include <cstring>
+
+#include "nv4_device.cuh"
+#include "nv4_launch.h"
+
+namespace nv4 {
+
+struct W4A16TcArgs {
+  const uint32_t* qz;      // int32 [K/128, N/8]
+  const uint16_t* scales;  // fp16 [K/128, N]
+  uint16_t* out;           // bf16 [M, N]
+  int M, N, K;
+  int tiles_m, tiles;      // token blocks; tiles (token blocks fastest)
+};
+
+constexpr int kD2Chunk = 64;          // K per pipeline chunk
+constexpr int kD2DequantWarps = 4;    // one per TMEM lane quarter
+constexpr int kD2EpiWarps = 16;       // four per lane quarter
+constexpr int kD2FirstEpiWarp = 2 + kD2DequantWarps;
+constexpr int kD2Threads = 32 * (kD2FirstEpiWarp + kD2EpiWarps);
+constexpr uint32_t kD2ACol = 256;     // first TMEM column of the A buffers
+
+template <int BN>
+struct D2Layout {
+  static constexpr int kStages = BN == 256 ? 5 : 8;  // at most 8 A buffers of 32 columns
+  static constexpr int kX = BN * 128;                 // x tile: BN rows of 64 BF16
+  static constexpr int kW = 8 * 128 * 4;              // packed weights: 8 rows of 128 int32
+  static constexpr int kStage = kX + kW;              // a multiple of 1024 (SW128 atoms)
+  static constexpr int kAcc = 256 / BN;               // accumulators
+  static constexpr int kBar = kStages * kStage;
+  // full[S], afull[S], consumed[S], tfull[A], tfree[A], done, tmem slot
+  static constexpr int kTotal = kBar + (3 * kStages + 2 * kAcc + 1) * 8 + 16;
+};
+
+// Instruction descriptor of tcgen05.mma kind::f16: BF16 A and B, both K-major,
+// FP32 accumulator, M x N.
+__host__ __device__ constexpr uint32_t umma_idesc_bf16(int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// D[tmem] (+)= A[tmem] * B[smem]^T, BF16 operands, A in tensor memory.
+__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.u32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 32 lanes x 32 columns of 32-bit TMEM -> 32 registers per thread.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+// The packed word w holds k0..k7 of one column (k_i in nibble i).  Returns the
+// BF16 pairs (k0, k1), (k2, k3), (k4, k5), (k6, k7) of bf16(128 + nibble): the
+// nibble fills the low mantissa bits of bf16(128) = 0x4300.
+__device__ __forceinline__ void nib_pairs_128(uint32_t w, uint32_t (&p)[4]) {
+  p[0] = (w & 0x0000000Fu) | ((w << 12) & 0x000F0000u) | 0x43004300u;
+  p[1] = ((w >> 8) & 0x0000000Fu) | ((w << 4) & 0x000F0000u) | 0x43004300u;
+  p[2] = ((w >> 16) & 0x0000000Fu) | ((w >> 4) & 0x000F0000u) | 0x43004300u;
+  p[3] = ((w >> 24) & 0x0000000Fu) | ((w >> 12) & 0x000F0000u) | 0x43004300u;
+}
+
+__device__ __forceinline__ uint32_t bf16x2_sub_u(uint32_t a, uint32_t b) {
+  __nv_bfloat162 r = __hsub2(*reinterpret_cast<__nv_bfloat162*>(&a), *reinterpret_cast<__nv_bfloat162*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+
+__device__ __forceinline__ uint32_t bf16x2_mul_u(uint32_t a, uint32_t b) {
+  __nv_bfloat162 r = __hmul2(*reinterpret_cast<__nv_bfloat162*>(&a), *reinterpret_cast<__nv_bfloat162*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+
+// Bounded wait used on the way out (also after an error was recorded).
+__device__ __forceinline__ bool mbar_wait_drain_d2(uint64_t* bar, uint32_t parity) {
+  const uint64_t start = global_timer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_timer_ns() - start > kWaitLimitNs) {
+      record_error(kErrTimeoutDrain);
+      return false;
+    }
+  }
+  return true;
+}
+
+// (129 + z) and the BF16-rounded scale of column n in group g, each as a BF16 pair.
+__device__ __forceinline__ void d2_zero_scale(const W4A16TcArgs& p, int g, int n, uint32_t& cz, uint32_t& s2) {
+  const int nc = min(n, p.N - 1);  // columns past N compute on a valid column and store nothing
+  const uint32_t zw = __ldg(p.qz + static_cast<size_t>(g) * (p.N / 8) + (nc >> 3));
+  const uint32_t z = (zw >> (4 * (nc & 7))) & 15u;
+  const uint32_t czb = __bfloat16_as_ushort(__float2bfloat16_rn(static_cast<float>(129u + z)));
+  cz = czb | (czb << 16);
+  const __half h = __ushort_as_half(__ldg(p.scales + static_cast<size_t>(g) * p.N + nc));
+  const uint32_t sb = __bfloat16_as_ushort(__float2bfloat16_rn(__half2float(h)));
+  s2 = sb | (sb << 16);
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kD2Threads, 1)
+    w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_qw,
+                    const W4A16TcArgs p) {
+  using L = D2Layout<BN>;
+  constexpr int S = L::kStages, NA = L::kAcc;
+  constexpr uint32_t IDESC = umma_idesc_bf16(128, BN);
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBar);
+  uint64_t* afull = full + S;
+  uint64_t* consumed = afull + S;
+  uint64_t* tfull = consumed + S;
+  uint64_t* tfree = tfull + NA;
+  uint64_t* done_bar = tfree + NA;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int KC = p.K / kD2Chunk;  // chunks per tile
+  const int my_tiles = p.tiles > static_cast<int>(blockIdx.x)
+                           ? (p.tiles - static_cast<int>(blockIdx.x) + gridDim.x - 1) / gridDim.x : 0;
+  const int total = my_tiles * KC;
+  auto tile_of = [&](int i) { return static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x); };
+  grid_dependents_launch();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&afull[s], kD2DequantWarps);
+      mbar_init(&consumed[s], 1);
+    }
+    for (int i = 0; i < NA; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tfree[i], kD2EpiWarps);
+    }
+    mbar_init(done_bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool ok = true;
+
+  if (warp == 0) {
+    // ---------------- TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmap_x);
+      tma_prefetch_desc(&tmap_qw);
+      const uint64_t wpol = policy_evict_first();
+      auto load_w = [&](int c) {  // first of a slot's two copies: expects both
+        const int s = c % S, t = tile_of(c / KC), kc = c % KC;
+        mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(L::kStage));
+        tma_load_2d_hint(smem + s * L::kStage + L::kX, &tmap_qw, &full[s], (t / p.tiles_m) * 128, kc * 8, wpol);
+      };
+      auto load_x = [&](int c) {
+        const int s = c % S, t = tile_of(c / KC), kc = c % KC;
+        tma_load_2d(smem + s * L::kStage, &tmap_x, &full[s], kc * kD2Chunk, (t % p.tiles_m) * BN);
+      };
+      // the first chunks' weights stream while the preceding kernel finishes
+      const int first = min(S, total);
+      for (int c = 0; c < first; ++c) load_w(c);
+      grid_dependency_wait();  // the activations come from the preceding kernel
+      for (int c = 0; c < first; ++c) load_x(c);
+      int issued = first;
+      for (int c = first; c < total; ++c) {
+        const int s = c % S;
+        if (!mbar_wait(&consumed[s], ((c / S) - 1) & 1, kErrTimeoutEmpty)) break;
+        load_w(c);
+        load_x(c);
+        issued = c + 1;
+      }
+      // every copy issued must land before the CTA may exit
+      for (int c = max(0, issued - S); c < issued; ++c)
+        if (!mbar_wait_drain_d2(&full[c % S], (c / S) & 1)) break;
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer: 4 x (M=128 columns, N=BN tokens, K=16) per chunk
+    if (lane == 0) {
+      const uint32_t stage_base = smem_u32(smem);
+      for (int c = 0; c < total && ok; ++c) {
+        const int s = c % S, ti = c / KC, kc = c % KC, b = ti % NA;
+        if (kc == 0) ok = mbar_wait(&tfree[b], (ti / NA) & 1, kErrTimeoutMma);
+        // afull[s] implies full[s]: the dequant warps waited for both copies
+        ok = ok && mbar_wait(&afull[s], (c / S) & 1, kErrTimeoutMma);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t x_addr = stage_base + s * L::kStage;
+        const uint32_t a_tmem = tmem + kD2ACol + 32u * s;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          umma_bf16_ts(tmem + b * BN, a_tmem + 8u * j, umma_desc_sw128(x_addr + 32 * j), IDESC,
+                       (kc > 0 || j > 0) ? 1u : 0u);
+        umma_commit(&consumed[s]);
+        if (kc == KC - 1) umma_commit(&tfull[b]);
+      }
+      // all issued MMAs must finish before the TMEM is released
+      umma_commit(done_bar);
+      mbar_wait(done_bar, 0, kErrTimeoutDrain);
+    }
+  } else if (warp < kD2FirstEpiWarp) {
+    // ---------------- dequantisation: thread = weight column (its TMEM lane)
+    const int quarter = warp & 3;
+    const int col = quarter * 32 + lane;
+    const uint32_t a_lane = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + kD2ACol;
+    uint32_t cz = 0, s2 = 0, cz_next = 0, s2_next = 0;
+    auto fetch = [&](int c) {  // zero point and scale of chunk c's group, loaded a group ahead
+      if (c >= total) return;
+      const int t = tile_of(c / KC), kc = c % KC;
+      d2_zero_scale(p, (kc * kD2Chunk) / 128, (t / p.tiles_m) * 128 + col, cz_next, s2_next);
+    };
+    fetch(0);
+    for (int c = 0; c < total && ok; ++c) {
+      const int s = c % S, kc = c % KC;
+      if ((kc & 1) == 0) {  // a new 128-group: take the prefetched pair, fetch the next group's
+        cz = cz_next;
+        s2 = s2_next;
+        fetch(c + 2);
+      }
+      ok = mbar_wait(&full[s], (c / S) & 1, kErrTimeoutFull);
+      if (!ok) break;
+      const uint32_t* wq = reinterpret_cast<const uint32_t*>(smem + s * L::kStage + L::kX);
+      uint32_t w[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) w[r] = wq[r * 128 + col];
+      uint32_t v[32];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        uint32_t pr[4];
+        nib_pairs_128(w[r], pr);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[r * 4 + j] = bf16x2_mul_u(bf16x2_sub_u(pr[j], cz), s2);
+      }
+      tmem_st32(a_lane + 32u * s, v);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&afull[s]);
+    }
+  } else {
+    // ---------------- epilogue: thread = weight column, BN/4 token columns
+    constexpr int kCols = BN / 4;
+    const int ew = warp - kD2FirstEpiWarp;
+    const int quarter = warp & 3;
+    const int c0 = (ew >> 2) * kCols;
+    const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + c0;
+    __syncwarp();
+    if (lane == 0)
+      for (int b = 0; b < NA; ++b) mbar_arrive(&tfree[b]);  // every accumulator starts free
+    for (int ti = 0; ti < my_tiles && ok; ++ti) {
+      const int b = ti % NA;
+      ok = mbar_wait(&tfull[b], (ti / NA) & 1, kErrTimeoutMma);
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t v[kCols];
+#pragma unroll
+      for (int c = 0; c < kCols; c += 32) tmem_ld32(taddr + b * BN + c, v + c);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tfree[b]);  // the accumulator goes back before the stores
+      const int t = tile_of(ti);
+      const int n = (t / p.tiles_m) * 128 + quarter * 32 + lane;
+      const int m0 = (t % p.tiles_m) * BN + c0;
+      if (n < p.N) {
+#pragma unroll
+        for (int j = 0; j < kCols; ++j) {
+          const int m = m0 + j;
+          if (m < p.M) p.out[static_cast<size_t>(m) * p.N + n] = __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[j])));
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------ host side
+template <int BN>
+static int launch_w4a16_tc_t(const CUtensorMap* maps, const W4A16TcArgs& a, int sms, cudaStream_t stream) {
+  static int done[64] = {};
+  auto* kern = &w4a16_tc_kernel<BN>;
+  const int smem = D2Layout<BN>::kTotal + 1024;
+  const int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem, done);
+  if (rc != NV4_OK) return rc;
+  const dim3 grid(static_cast<unsigned>(std::min<int64_t>(a.tiles, sms)));
+  return launch_kernel(kern, grid, dim3(kD2Threads), smem, stream, true, maps[0], maps[1], a);
+}
+
+// Token tiles of 256 when there are enough tokens to fill them, else 128.
+// Shapes outside the kernel's alignment rules return NV4_ERR_UNSUPPORTED (the
+// caller then takes the mma.sync kernel).
+int launch_w4a16_tc_gemm(const void* x, const void* qweight, const void* qzeros, const void* scales, void* out,
+                         int64_t m, int64_t n, int64_t k, cudaStream_t stream) {
+  if (m < 1 || n < 8 || n % 8 || k < 128 || k % 128 || (reinterpret_cast<uintptr_t>(x) & 15) ||
+      (reinterpret_cast<uintptr_t>(qweight) & 15) || m > (int64_t(1) << 30) || n > (int64_t(1) << 30))
+    return NV4_ERR_UNSUPPORTED;
+  const int sms = device_sm_count();
+  if (sms <= 0) return NV4_ERR_CUDA;
+  const int bn = m > 128 ? 256 : 128;
+  CUtensorMap maps[2];
+  memset(maps, 0, sizeof(maps));
+  const bool okm = make_tensor_map_2d(&maps[0], CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, x, static_cast<uint64_t>(m),
+                                      static_cast<uint64_t>(k), static_cast<uint32_t>(bn), kD2Chunk,
+                                      CU_TENSOR_MAP_SWIZZLE_128B) &&
+                   make_tensor_map_2d(&maps[1], CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, qweight, static_cast<uint64_t>(k / 8),
+                                      static_cast<uint64_t>(n), 8, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (!okm) return NV4_ERR_CUDA;
+  W4A16TcArgs a;
+  a.qz = static_cast<const uint32_t*>(qzeros);
+  a.scales = static_cast<const uint16_t*>(scales);
+  a.out = static_cast<uint16_t*>(out);
+  a.M = static_cast<int>(m);
+  a.N = static_cast<int>(n);
+  a.K = static_cast<int>(k);
+  a.tiles_m = static_cast<int>((m + bn - 1) / bn);
+  const int64_t tiles = ((n + 127) / 128) * a.tiles_m;
+  if (tiles > (int64_t(1) << 30)) return NV4_ERR_UNSUPPORTED;
+  a.tiles = static_cast<int>(tiles);
+  return bn == 256 ? launch_w4a16_tc_t<256>(maps, a, sms, stream) : launch_w4a16_tc_t<128>(maps, a, sms, stream);
+}
+
+}  // namespace nv4

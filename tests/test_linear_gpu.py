@@ -133,6 +133,30 @@ def test_w4a16_matches_oracle(cuda_device, n, k, m):
     assert rel_b < 1e-3, rel_b      # same BF16 rounding as the exact product, up to FP32 sums
 
 
+@pytest.mark.parametrize("m,n,k", [(33, 192, 512), (300, 320, 1024), (257, 4096, 12288), (2048, 24576, 4096)])
+def test_w4a16_prefill_tiles(cuda_device, m, n, k):
+    """The tcgen05 W4A16 kernel (more than 32 tokens): ragged token and column
+    tiles (zero-filled TMA boxes past M and N, stores masked) and a full
+    config-3 prefill shape, on a sample of rows against the float64 oracle."""
+    qweight, qzeros, scales = synthetic.w4a16_weights(n, k, seed=7 * n + k)
+    layer = W4A16Linear(k, n).to(cuda_device)
+    with torch.no_grad():
+        layer.qweight.copy_(qweight)
+        layer.qzeros.copy_(qzeros)
+        layer.scales.copy_(scales)
+    x = synthetic.activations(m, k, seed=m + 5)
+    out = torch.full((m + 1, n), float("nan"), dtype=torch.bfloat16, device=cuda_device)
+    out[:m].copy_(layer(x.to(cuda_device)))
+    got = out.float().cpu().numpy().astype(np.float64)
+    assert np.isnan(got[m]).all()  # the guard row is untouched
+    rows = np.unique(np.concatenate([np.arange(0, m, max(1, m // 24)), [m - 1]]))
+    expected = o.w4a16_gemm_f64(u16(x[rows]), qweight.numpy(), qzeros.numpy(), scales.numpy())
+    rel = np.linalg.norm(got[rows] - expected) / np.linalg.norm(expected)
+    assert rel < 4e-3, rel
+    exp_bf16 = o.round_to_bf16(expected.astype(np.float32)).astype(np.float64)
+    assert np.linalg.norm(got[rows] - exp_bf16) / np.linalg.norm(expected) < 1e-3
+
+
 def test_w4a16_large_m_and_graph(cuda_device):
     n, k, m = 6144, 4096, 2048
     qweight, qzeros, scales = synthetic.w4a16_weights(n, k, seed=1)
