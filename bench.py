@@ -566,6 +566,62 @@ def measure_model(world: int, prompt_len: int = E2E_PROMPT, decode: int = E2E_DE
     return out
 
 
+# ---------------------------------------------------------------- one kernel (profiling)
+def run_kernel(spec: str, reps: int) -> None:
+    """``--kernel NAME:MxNxK``: one kernel on one shape, a few warm-up launches
+    and `reps` timed ones (the small, self-contained command the ncu summaries
+    in profiles/ are captured from).  NAME is w4a4 (activation prep + grouped
+    GEMM; M > 64 takes the tcgen05 prefill kernel, fewer tokens the decode
+    kernel) or w4a16 (W4A16Linear)."""
+    name, shape = spec.split(":")
+    m, n, k = (int(v) for v in shape.lower().split("x"))
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    g = torch.Generator(device=device).manual_seed(1)
+    x = torch.randn(m, k, device=device, generator=g).bfloat16()
+    if name == "w4a4":
+        from nanovllm.kernels.w4a4_grouped_kernel import w4a4_grouped_gemm_i8
+        from nanovllm.layers.linear_w4a4 import W4A4Linear
+        mod = W4A4Linear(k, n, layout="block128", clamp_lo=-8).to(device)
+        packed = torch.randint(-128, 128, (n, k // 2), dtype=torch.int8, device=device, generator=g)
+        scale = (torch.randn(n, k // 128, device=device, generator=g).abs() * (0.02 / 7)).bfloat16()
+        signs = torch.randint(0, 2, (k,), device=device, generator=g, dtype=torch.int8) * 2 - 1
+        mod.load_full(packed, scale, signs)
+        codes, sa = mod.quantize_input(x)
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=device)
+
+        def call():
+            w4a4_grouped_gemm_i8(codes, mod.packed_weight, sa, mod.weight_scale, out=out)
+        work, unit = 2 * m * n * k / 1e12, "TOPS"
+    elif name == "w4a16":
+        from nanovllm.layers.linear_w4a16 import W4A16Linear
+        lin = W4A16Linear(k, n).to(device)
+        with torch.no_grad():
+            lin.qweight.copy_(torch.randint(-2 ** 31, 2 ** 31 - 1, lin.qweight.shape, dtype=torch.int64,
+                                            device=device, generator=g).to(torch.int32))
+            lin.qzeros.copy_(torch.randint(-2 ** 31, 2 ** 31 - 1, lin.qzeros.shape, dtype=torch.int64,
+                                           device=device, generator=g).to(torch.int32))
+            lin.scales.copy_((torch.randn(lin.scales.shape, device=device, generator=g).abs() * 0.02).half())
+
+        def call():
+            lin(x)
+        work, unit = 2 * m * n * k / 1e12, "TFLOPS"
+    else:
+        raise SystemExit(f"unknown kernel {name!r} (w4a4 or w4a16)")
+    with torch.no_grad():
+        for _ in range(3):
+            call()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(reps):
+            call()
+        end.record()
+        end.synchronize()
+    t = start.elapsed_time(end) / 1e3 / reps
+    print(json.dumps({"kernel": spec, "us_per_call": t * 1e6, unit.lower(): work / t}), flush=True)
+
+
 # ---------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser(description=__doc__)
@@ -579,8 +635,13 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the per-config measurements (1 GPU)")
     ap.add_argument("--no-model", action="store_true", help="skip the end-to-end model (config 4)")
+    ap.add_argument("--kernel", default=None, metavar="NAME:MxNxK",
+                    help="time one kernel on one shape (w4a4 or w4a16), e.g. w4a4:4096x24576x4096; the command "
+                         "the ncu summaries in profiles/ are captured from")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.kernel:
+        return run_kernel(args.kernel, max(1, args.steps if args.steps != 200 else 10))
     if args.impl == "reference":
         return run_reference(args)
 

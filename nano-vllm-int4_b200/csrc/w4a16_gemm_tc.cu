@@ -16,15 +16,20 @@
 //       exactly as TMA lands them.
 // Persistent: one CTA per SM walks tiles of 128 weight columns x BN tokens
 // over all of K, 64 K per pipeline chunk:
-//   warp 0      TMA producer: x tile [BN x 64 k] and the packed weight tile
-//               [8 rows of k/8 x 128 columns] per chunk into an S-slot ring.
+//   warp 0      TMA producer: per chunk, the x tile [BN x 64 k], the packed
+//               weight tile [8 rows of k/8 x 128 columns] and the chunk's group
+//               row of scales [128] and zero points [16 words] into an S-slot
+//               ring (no global loads on the dequantisation path).
 //   warp 1      TMEM allocation (all 512 columns) and the single MMA-issuing
 //               thread: 4 x tcgen05.mma kind::f16 (K = 16) per chunk.
-//   warps 2-5   dequantisation, one warp per TMEM lane quarter: thread = weight
-//               column; 8 packed words -> 32 BF16 pairs -> tcgen05.st into the
-//               chunk's A buffer.
-//   warps 6-21  epilogue, four per lane quarter (BN/4 tokens each): tcgen05.ld,
-//               hand the accumulator back, round to BF16, store out[t, n].
+//   warps 2-9   dequantisation, two warps per TMEM lane quarter taking
+//               alternate chunks: thread = weight column; 8 packed words -> 32
+//               BF16 pairs -> tcgen05.st into the chunk's A buffer.  (The
+//               dequantisation is the kernel's busiest ALU work; two warps per
+//               sub-partition keep it ahead of the tensor core.)
+//   warps 10-25 epilogue, four per lane quarter (BN/4 tokens each, 32 at a
+//               time): tcgen05.ld, round to BF16, store out[t, n], then hand the
+//               accumulator back.
 // TMEM columns: accumulators [0, 256) (one of 256 tokens or two of 128), A
 // buffers [256, 512) (32 columns per chunk, up to 8).
 //
@@ -38,15 +43,13 @@
 namespace nv4 {
 
 struct W4A16TcArgs {
-  const uint32_t* qz;      // int32 [K/128, N/8]
-  const uint16_t* scales;  // fp16 [K/128, N]
   uint16_t* out;           // bf16 [M, N]
   int M, N, K;
   int tiles_m, tiles;      // token blocks; tiles (token blocks fastest)
 };
 
 constexpr int kD2Chunk = 64;          // K per pipeline chunk
-constexpr int kD2DequantWarps = 4;    // one per TMEM lane quarter
+constexpr int kD2DequantWarps = 8;    // two per TMEM lane quarter (alternate chunks)
 constexpr int kD2EpiWarps = 16;       // four per lane quarter
 constexpr int kD2FirstEpiWarp = 2 + kD2DequantWarps;
 constexpr int kD2Threads = 32 * (kD2FirstEpiWarp + kD2EpiWarps);
@@ -57,7 +60,10 @@ struct D2Layout {
   static constexpr int kStages = BN == 256 ? 5 : 8;  // at most 8 A buffers of 32 columns
   static constexpr int kX = BN * 128;                 // x tile: BN rows of 64 BF16
   static constexpr int kW = 8 * 128 * 4;              // packed weights: 8 rows of 128 int32
-  static constexpr int kStage = kX + kW;              // a multiple of 1024 (SW128 atoms)
+  static constexpr int kS = 128 * 2;                  // the group's scales of the 128 columns (fp16)
+  static constexpr int kZ = 16 * 4;                   // the group's zero-point words of the 128 columns
+  static constexpr int kBytes = kX + kW + kS + kZ;    // TMA bytes per stage
+  static constexpr int kStage = (kBytes + 1023) & ~1023;  // a multiple of 1024 (SW128 atoms)
   static constexpr int kAcc = 256 / BN;               // accumulators
   static constexpr int kBar = kStages * kStage;
   // full[S], afull[S], consumed[S], tfull[A], tfree[A], done, tmem slot
@@ -125,21 +131,22 @@ __device__ __forceinline__ bool mbar_wait_drain_d2(uint64_t* bar, uint32_t parit
   return true;
 }
 
-// (129 + z) and the BF16-rounded scale of column n in group g, each as a BF16 pair.
-__device__ __forceinline__ void d2_zero_scale(const W4A16TcArgs& p, int g, int n, uint32_t& cz, uint32_t& s2) {
-  const int nc = min(n, p.N - 1);  // columns past N compute on a valid column and store nothing
-  const uint32_t zw = __ldg(p.qz + static_cast<size_t>(g) * (p.N / 8) + (nc >> 3));
-  const uint32_t z = (zw >> (4 * (nc & 7))) & 15u;
+// (129 + z) and the BF16-rounded scale of column `col` of the tile, each as a
+// BF16 pair, from the stage's scale row and zero-point words.
+__device__ __forceinline__ void d2_zero_scale(const uint8_t* stage_zs, int col, uint32_t& cz, uint32_t& s2) {
+  const uint16_t* sc = reinterpret_cast<const uint16_t*>(stage_zs);
+  const uint32_t* zw = reinterpret_cast<const uint32_t*>(stage_zs + 256);
+  const uint32_t z = (zw[col >> 3] >> (4 * (col & 7))) & 15u;
   const uint32_t czb = __bfloat16_as_ushort(__float2bfloat16_rn(static_cast<float>(129u + z)));
   cz = czb | (czb << 16);
-  const __half h = __ushort_as_half(__ldg(p.scales + static_cast<size_t>(g) * p.N + nc));
-  const uint32_t sb = __bfloat16_as_ushort(__float2bfloat16_rn(__half2float(h)));
+  const uint32_t sb = __bfloat16_as_ushort(__float2bfloat16_rn(__half2float(__ushort_as_half(sc[col]))));
   s2 = sb | (sb << 16);
 }
 
 template <int BN>
 __global__ void __launch_bounds__(kD2Threads, 1)
     w4a16_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_qw,
+                    const __grid_constant__ CUtensorMap tmap_sc, const __grid_constant__ CUtensorMap tmap_qz,
                     const W4A16TcArgs p) {
   using L = D2Layout<BN>;
   constexpr int S = L::kStages, NA = L::kAcc;
@@ -166,7 +173,7 @@ __global__ void __launch_bounds__(kD2Threads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&afull[s], kD2DequantWarps);
+      mbar_init(&afull[s], kD2DequantWarps / 2);  // the four warps of the chunk's parity
       mbar_init(&consumed[s], 1);
     }
     for (int i = 0; i < NA; ++i) {
@@ -191,11 +198,16 @@ __global__ void __launch_bounds__(kD2Threads, 1)
     if (lane == 0) {
       tma_prefetch_desc(&tmap_x);
       tma_prefetch_desc(&tmap_qw);
+      tma_prefetch_desc(&tmap_sc);
+      tma_prefetch_desc(&tmap_qz);
       const uint64_t wpol = policy_evict_first();
-      auto load_w = [&](int c) {  // first of a slot's two copies: expects both
-        const int s = c % S, t = tile_of(c / KC), kc = c % KC;
-        mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(L::kStage));
-        tma_load_2d_hint(smem + s * L::kStage + L::kX, &tmap_qw, &full[s], (t / p.tiles_m) * 128, kc * 8, wpol);
+      auto load_w = [&](int c) {  // first of a slot's copies: expects all of them
+        const int s = c % S, t = tile_of(c / KC), kc = c % KC, n0 = (t / p.tiles_m) * 128;
+        uint8_t* st = smem + s * L::kStage;
+        mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(L::kBytes));
+        tma_load_2d_hint(st + L::kX, &tmap_qw, &full[s], n0, kc * 8, wpol);
+        tma_load_2d(st + L::kX + L::kW, &tmap_sc, &full[s], n0, (kc * kD2Chunk) / 128);
+        tma_load_2d(st + L::kX + L::kW + L::kS, &tmap_qz, &full[s], n0 / 8, (kc * kD2Chunk) / 128);
       };
       auto load_x = [&](int c) {
         const int s = c % S, t = tile_of(c / KC), kc = c % KC;
@@ -243,27 +255,20 @@ __global__ void __launch_bounds__(kD2Threads, 1)
       mbar_wait(done_bar, 0, kErrTimeoutDrain);
     }
   } else if (warp < kD2FirstEpiWarp) {
-    // ---------------- dequantisation: thread = weight column (its TMEM lane)
+    // ---------------- dequantisation: thread = weight column (its TMEM lane);
+    // the two warps of a lane quarter take alternate chunks
     const int quarter = warp & 3;
+    const int parity = (warp - 2) >> 2;
     const int col = quarter * 32 + lane;
     const uint32_t a_lane = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + kD2ACol;
-    uint32_t cz = 0, s2 = 0, cz_next = 0, s2_next = 0;
-    auto fetch = [&](int c) {  // zero point and scale of chunk c's group, loaded a group ahead
-      if (c >= total) return;
-      const int t = tile_of(c / KC), kc = c % KC;
-      d2_zero_scale(p, (kc * kD2Chunk) / 128, (t / p.tiles_m) * 128 + col, cz_next, s2_next);
-    };
-    fetch(0);
-    for (int c = 0; c < total && ok; ++c) {
-      const int s = c % S, kc = c % KC;
-      if ((kc & 1) == 0) {  // a new 128-group: take the prefetched pair, fetch the next group's
-        cz = cz_next;
-        s2 = s2_next;
-        fetch(c + 2);
-      }
-      ok = mbar_wait(&full[s], (c / S) & 1, kErrTimeoutFull);
+    for (int c = parity; c < total && ok; c += 2) {
+      const int s = c % S;
+      ok = __all_sync(0xffffffffu, mbar_wait(&full[s], (c / S) & 1, kErrTimeoutFull));
       if (!ok) break;
-      const uint32_t* wq = reinterpret_cast<const uint32_t*>(smem + s * L::kStage + L::kX);
+      const uint8_t* st = smem + s * L::kStage;
+      const uint32_t* wq = reinterpret_cast<const uint32_t*>(st + L::kX);
+      uint32_t cz, s2;
+      d2_zero_scale(st + L::kX + L::kW, col, cz, s2);
       uint32_t w[8];
 #pragma unroll
       for (int r = 0; r < 8; ++r) w[r] = wq[r * 128 + col];
@@ -296,23 +301,26 @@ __global__ void __launch_bounds__(kD2Threads, 1)
       ok = mbar_wait(&tfull[b], (ti / NA) & 1, kErrTimeoutMma);
       if (!ok) break;
       tc_fence_after();
-      uint32_t v[kCols];
-#pragma unroll
-      for (int c = 0; c < kCols; c += 32) tmem_ld32(taddr + b * BN + c, v + c);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tfree[b]);  // the accumulator goes back before the stores
       const int t = tile_of(ti);
       const int n = (t / p.tiles_m) * 128 + quarter * 32 + lane;
       const int m0 = (t % p.tiles_m) * BN + c0;
-      if (n < p.N) {
 #pragma unroll
-        for (int j = 0; j < kCols; ++j) {
-          const int m = m0 + j;
-          if (m < p.M) p.out[static_cast<size_t>(m) * p.N + n] = __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[j])));
+      for (int c = 0; c < kCols; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(taddr + b * BN + c, v);
+        tmem_wait_ld();
+        if (n < p.N) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int m = m0 + c + j;
+            if (m < p.M)
+              p.out[static_cast<size_t>(m) * p.N + n] = __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[j])));
+          }
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tfree[b]);
     }
   }
   tc_fence_before();
@@ -332,7 +340,7 @@ static int launch_w4a16_tc_t(const CUtensorMap* maps, const W4A16TcArgs& a, int 
   const int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem, done);
   if (rc != NV4_OK) return rc;
   const dim3 grid(static_cast<unsigned>(std::min<int64_t>(a.tiles, sms)));
-  return launch_kernel(kern, grid, dim3(kD2Threads), smem, stream, true, maps[0], maps[1], a);
+  return launch_kernel(kern, grid, dim3(kD2Threads), smem, stream, true, maps[0], maps[1], maps[2], maps[3], a);
 }
 
 // Token tiles of 256 when there are enough tokens to fill them, else 128.
@@ -340,23 +348,26 @@ static int launch_w4a16_tc_t(const CUtensorMap* maps, const W4A16TcArgs& a, int 
 // caller then takes the mma.sync kernel).
 int launch_w4a16_tc_gemm(const void* x, const void* qweight, const void* qzeros, const void* scales, void* out,
                          int64_t m, int64_t n, int64_t k, cudaStream_t stream) {
-  if (m < 1 || n < 8 || n % 8 || k < 128 || k % 128 || (reinterpret_cast<uintptr_t>(x) & 15) ||
-      (reinterpret_cast<uintptr_t>(qweight) & 15) || m > (int64_t(1) << 30) || n > (int64_t(1) << 30))
+  if (m < 1 || n < 32 || n % 32 || k < 128 || k % 128 || (reinterpret_cast<uintptr_t>(x) & 15) ||
+      (reinterpret_cast<uintptr_t>(qweight) & 15) || (reinterpret_cast<uintptr_t>(qzeros) & 15) ||
+      (reinterpret_cast<uintptr_t>(scales) & 15) || m > (int64_t(1) << 30) || n > (int64_t(1) << 30))
     return NV4_ERR_UNSUPPORTED;
   const int sms = device_sm_count();
   if (sms <= 0) return NV4_ERR_CUDA;
   const int bn = m > 128 ? 256 : 128;
-  CUtensorMap maps[2];
+  CUtensorMap maps[4];
   memset(maps, 0, sizeof(maps));
   const bool okm = make_tensor_map_2d(&maps[0], CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, x, static_cast<uint64_t>(m),
                                       static_cast<uint64_t>(k), static_cast<uint32_t>(bn), kD2Chunk,
                                       CU_TENSOR_MAP_SWIZZLE_128B) &&
                    make_tensor_map_2d(&maps[1], CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, qweight, static_cast<uint64_t>(k / 8),
-                                      static_cast<uint64_t>(n), 8, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+                                      static_cast<uint64_t>(n), 8, 128, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+                   make_tensor_map_2d(&maps[2], CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, scales, static_cast<uint64_t>(k / 128),
+                                      static_cast<uint64_t>(n), 1, 128, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+                   make_tensor_map_2d(&maps[3], CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, qzeros, static_cast<uint64_t>(k / 128),
+                                      static_cast<uint64_t>(n / 8), 1, 16, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (!okm) return NV4_ERR_CUDA;
   W4A16TcArgs a;
-  a.qz = static_cast<const uint32_t*>(qzeros);
-  a.scales = static_cast<const uint16_t*>(scales);
   a.out = static_cast<uint16_t*>(out);
   a.M = static_cast<int>(m);
   a.N = static_cast<int>(n);
