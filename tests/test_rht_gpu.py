@@ -15,7 +15,7 @@ import pytest
 import torch
 
 import cases
-from gpu_helpers import Guarded, u16, u8
+from gpu_helpers import Guarded, assert_prep_matches, u16, u8
 from nanovllm import _native
 from nanovllm.kernels.rht_a4_tilelang import rht_quant_pack
 from nanovllm.utils import synthetic
@@ -42,9 +42,7 @@ def run_kernel(x, signs, layout, lo):
 
 def assert_matches_oracle(x_cpu, signs_cpu, packed, sbits, layout, lo):
     ref_packed, ref_sbits, _, _, _ = o.prepare(u16(x_cpu), signs_cpu.numpy(), LAYOUTS[layout], lo)
-    mism_codes = int((o.unpack_int4(packed) != o.unpack_int4(ref_packed)).sum())
-    mism_scales = int((sbits != ref_sbits).sum())
-    assert mism_codes == 0 and mism_scales == 0, f"{mism_codes} codes and {mism_scales} scales differ from the oracle"
+    assert_prep_matches(packed, sbits, ref_packed, ref_sbits, o.unpack_int4)
 
 
 @pytest.mark.parametrize("layout,lo", [("block128", -8), ("block128", -7), ("row_DH", -7), ("row_DH", -8)])
