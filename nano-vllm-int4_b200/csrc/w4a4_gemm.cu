@@ -89,8 +89,9 @@ __device__ __forceinline__ bool scale_in_fast_range(float s, float lo, float hi)
 
 // Shared-memory carve-up (byte offsets from the 1024-aligned base).
 struct StreamLayout {
-  int w_bytes, a_bytes, stage_bytes, sw_off, sa_off, sac_off, flags_off, ds_off, bar_off, total;
-  __host__ __device__ StreamLayout(int R, int MP, int G, int S, bool wg, int ds_bytes) {
+  int w_bytes, a_bytes, stage_bytes, sw_off, sa_off, sac_off, flags_off, ds_off, pt_off, bar_off, total;
+  // pt_bytes: the FP32 output tile staged for the peer stores (peer mode), else 0
+  __host__ __device__ StreamLayout(int R, int MP, int G, int S, bool wg, int ds_bytes, int pt_bytes) {
     w_bytes = R * 128;
     a_bytes = MP * 128;  // per group (A8) or per stage (packed)
     stage_bytes = w_bytes + 2 * a_bytes;
@@ -100,7 +101,8 @@ struct StreamLayout {
     sac_off = (sa_off + MP * G * 2 + 15) & ~15;
     flags_off = sac_off + MP * G * 8;
     ds_off = (flags_off + (2 * G + 4) * 4 + 15) & ~15;  // K-split partials (KS > 1)
-    bar_off = (ds_off + ds_bytes + 7) & ~7;
+    pt_off = (ds_off + ds_bytes + 15) & ~15;
+    bar_off = (pt_off + pt_bytes + 7) & ~7;
     total = bar_off + (2 * S + 2) * 8 + 16;
   }
 };
@@ -126,7 +128,7 @@ __global__ void __launch_bounds__(32 * (kProducerWarps + (KS == 1 && TPW == MT ?
   const int S = p.stages, R = p.R, G = p.G;
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  const StreamLayout L(R, MP, G, S, WG, stream_ds_bytes(p.slabs * TS, KS, TPW));
+  const StreamLayout L(R, MP, G, S, WG, stream_ds_bytes(p.slabs * TS, KS, TPW), p.peer_world ? MP * R * 4 : 0);
   uint16_t* sw_s = reinterpret_cast<uint16_t*>(smem + L.sw_off);   // [R][G] (or [R])
   uint16_t* sa_s = reinterpret_cast<uint16_t*>(smem + L.sa_off);   // [MP][G]
   // [G][MP/2] float4 per token pair (t, t+1): (sa_t/16, sa_t+1/16, -786432*sa_t, -786432*sa_t+1)
@@ -367,14 +369,14 @@ __global__ void __launch_bounds__(32 * (kProducerWarps + (KS == 1 && TPW == MT ?
   };
 
   const int peer_parity = p.peer_world ? (fast_g[G + 1] & 1) : 0;
+  float* ptile = reinterpret_cast<float*>(smem + L.pt_off);  // peer mode: [MP tokens][R rows] FP32
   auto store_out = [&](int row, int tok, float v) {
     const int rr = n0 + row, tk = m0 + tok;
     if (tk < p.M && rr < p.N) {
       if (!WG) v = __fmul_rn(v, bf16_bits_to_f32(sw_s[row]));
       const size_t o = static_cast<size_t>(tk) * p.N + rr;
       if (p.peer_world) {
-        for (int r = 0; r < p.peer_world; ++r)
-          peer_inbox(p.peer_bufs[r], p.peer_capacity, peer_parity, p.peer_rank)[o] = v;
+        ptile[tok * R + row] = v;  // copied to the ranks' inboxes in 16-byte stores below
       } else if (F32)
         static_cast<float*>(p.out)[o] = v;
       else
@@ -643,9 +645,23 @@ __global__ void __launch_bounds__(32 * (kProducerWarps + (KS == 1 && TPW == MT ?
     }
   }
   if (p.peer_world) {
-    // every consumer's tile stores before one thread's system-scope release of
-    // this CTA's flag on each peer (released on error too, so that the peers
-    // do not wait out their limit; the error word marks the call as failed)
+    // The staged tile goes to every rank's inbox in 16-byte stores (whole
+    // token rows of the CTA's R columns; each CTA starts with a different
+    // rank, spreading the NVLink traffic), then, after every consumer's
+    // stores, one thread's system-scope release of this CTA's flag on each
+    // peer (released on error too, so that the peers do not wait out their
+    // limit; the error word marks the call as failed).
+    named_barrier_sync(1, cthreads);
+    const int wq = min(R, p.N - n0) >> 2, rows = min(MP, p.M - m0);
+    for (int j = 0; j < p.peer_world; ++j) {
+      const int r = (static_cast<int>(blockIdx.x) + j) % p.peer_world;
+      float* dst = peer_inbox(p.peer_bufs[r], p.peer_capacity, peer_parity, p.peer_rank);
+      for (int i = ct; i < rows * wq; i += cthreads) {
+        const int t = i / wq, c = i - t * wq;
+        *reinterpret_cast<float4*>(dst + static_cast<size_t>(m0 + t) * p.N + n0 + 4 * c) =
+            *reinterpret_cast<const float4*>(ptile + t * R + 4 * c);
+      }
+    }
     named_barrier_sync(1, cthreads);
     if (ct == 0) {
       const uint32_t e = static_cast<uint32_t>(fast_g[G + 1]);
@@ -741,7 +757,7 @@ int plan_w4a4_stream(int64_t m, int64_t n, int64_t k, bool wg, int sms, bool pee
   // from enough slabs per CTA for that (the ring rule may still lower it).
   if (peer) slabs = std::max<int>(slabs, static_cast<int>(std::min<int64_t>(kMaxWideSlabs, (total_slabs + kPeerSlots - 1) / kPeerSlots)));
   const int n_iters = (G + 1) / 2;
-  int ks = 0, ts = 1, tpw = MT, ds_bytes = 0, R = 0, stages = 0;
+  int ks = 0, ts = 1, tpw = MT, ds_bytes = 0, pt_bytes = 0, R = 0, stages = 0;
   for (;;) {
     ks = slabs <= 4 ? 4 : 1;
     if (ks == 1) slabs = std::min(slabs, kMaxWideSlabs);  // wider layers take more CTAs
@@ -750,7 +766,8 @@ int plan_w4a4_stream(int64_t m, int64_t n, int64_t k, bool wg, int sms, bool pee
     tpw = MT / ts;
     ds_bytes = stream_ds_bytes(slabs * ts, ks, tpw);
     R = slabs * 16;
-    const StreamLayout one(R, MP, G, 1, wg, ds_bytes);
+    pt_bytes = peer ? MP * R * 4 : 0;
+    const StreamLayout one(R, MP, G, 1, wg, ds_bytes, pt_bytes);
     const int fixed = one.total - one.stage_bytes;
     stages = (kSmemLimit - 1024 - fixed - 64) / (one.stage_bytes + 16);
     stages = std::min(stages, std::min(16, n_iters));
@@ -758,7 +775,7 @@ int plan_w4a4_stream(int64_t m, int64_t n, int64_t k, bool wg, int sms, bool pee
     slabs = slabs > 4 ? 4 : slabs - 1;
   }
   if (stages < 1 || stages < std::min(n_iters, ks + kProducerWarps)) return NV4_ERR_UNSUPPORTED;
-  const StreamLayout lay(R, MP, G, stages, wg, ds_bytes);
+  const StreamLayout lay(R, MP, G, stages, wg, ds_bytes, pt_bytes);
   StreamPlan pl;
   pl.token_tiles = MT;
   pl.slabs = slabs;
