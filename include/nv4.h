@@ -220,15 +220,12 @@ int nv4_peer_allreduce_bf16(void* const* bufs, int rank, int world, void* out, i
  * The row-parallel W4A4 GEMM and its all-reduce in two launches without the
  * FP32 partial round trip: the GEMM (GEMM-ready INT8 activation codes as in
  * nv4_w4a4_gemm_i8, up to NV4_PEER_MAX_TOKENS rows) stores each CTA's FP32
- * output tile straight into peer inboxes over NVLink and a second kernel sums
- * the ranks' tiles in rank order to BF16 [m, n] in `out` (16-byte aligned).
- * With 2 ranks every tile goes to every rank (one-shot); with more, tile j goes
- * only to its owner rank j % world, which sums it and stores the BF16 result
- * on every rank (two-shot, less NVLink traffic) -- the same values as
- * nv4_w4a4_gemm_i8 (FP32)
- * followed by nv4_peer_allreduce_bf16.  m * n must not exceed `capacity`;
- * flags: NV4_GEMM_W_SCALE_GROUPED only.  The two forms may share one set of
- * peer buffers; every rank makes the same sequence of calls.
+ * output tile straight into every rank's inbox over NVLink and releases one
+ * flag per CTA on each peer; a second kernel waits for the peers' tiles and
+ * sums them in rank order to BF16 [m, n] in `out` -- the same values as
+ * nv4_w4a4_gemm_i8 (FP32) followed by nv4_peer_allreduce_bf16.  m * n must not
+ * exceed `capacity`; flags: NV4_GEMM_W_SCALE_GROUPED only.  The two forms may
+ * share one set of peer buffers; every rank makes the same sequence of calls.
  */
 int nv4_w4a4_gemm_peer_allreduce_bf16(const void* a_codes, const void* w_packed, const void* a_scale,
                                       const void* w_scale, void* out, int64_t m, int64_t n, int64_t k, int flags,

@@ -12,22 +12,12 @@
 //   releases flag[rank][c] there, waits for its own flag[r][c] of every peer
 //   and sums the chunk in rank order 0 .. world-1.
 // E2, peer_reduce_tiles_bf16_kernel (after the row-parallel stream GEMM run in
-//   peer mode).  Up to kPeerOneShotMaxRanks ranks, one-shot: every rank's GEMM
-//   CTA j stored its [M x R] FP32 tile into inbox[parity][rank] of every rank
-//   and released flag[rank][j] on the peers; CTA j waits for the peers' flags
-//   and sums tile j in rank order.  Above that, two-shot: tile j has one owner,
-//   rank j % world.  Every rank's GEMM CTA j stored its FP32 tile into the
-//   owner's inbox[parity][rank] and released flag[rank][j] there (reduce-
-//   scatter).  On the owner, CTA j waits for the other ranks' flags, sums the
-//   tile in rank order, writes the BF16 result to its own output and to the
-//   result area of every other rank, and releases done[j] there; on the other
-//   ranks CTA j waits for done[j] and copies the tile (all-gather).  Each rank
-//   sends (world-1)/world of its FP32 partial and 1/world of the BF16 sum to
-//   each peer -- about world/3 times less than sending the whole partial to
-//   every peer, which SM-issued remote stores pay for at 8 ranks.
-// Both forms sum in the same order, so all ranks get identical BF16 (equal to
-// NCCL's two-rank sum at TP=2).  Every wait gives up after 2 s, records an
-// error word and returns.
+//   peer mode, whose CTA j stored its [M x R] FP32 tile into inbox[parity][rank]
+//   of every rank and released flag[rank][j] on the peers): CTA j waits for
+//   flag[r][j] of every peer and sums tile j in rank order.
+// Both sum in the same order on every rank, so all ranks get identical BF16
+// (equal to NCCL's two-rank sum at TP=2).  Every wait gives up after 2 s,
+// records an error word and returns.
 #include "nv4_device.cuh"
 #include "nv4_launch.h"
 #include "peer_common.cuh"
@@ -116,73 +106,47 @@ __global__ void __launch_bounds__(256) peer_reduce_tiles_bf16_kernel(const PeerT
   __shared__ uint32_t epoch_s;
   uint8_t* own = p.bufs[p.rank];
   const int j = blockIdx.x;
-  const int owner = j % p.world;
   grid_dependents_launch();
   grid_dependency_wait();  // the peer-mode GEMM of this call took the epoch and wrote this rank's tiles
   if (threadIdx.x == 0) epoch_s = peer_epochs(own)[j];
   __syncthreads();
   const uint32_t e = epoch_s;
   const int parity = static_cast<int>(e & 1u);
+  bool ok = true;
+  if (threadIdx.x < p.world && threadIdx.x != p.rank)
+    ok = peer_wait_flag(peer_flags(own) + threadIdx.x * kPeerSlots + j, e);
+  if (!__syncthreads_and(ok)) return;
   const int n0 = j * p.R, w = min(p.R, p.N - n0);
   if (w <= 0) return;
-  const int w8 = w >> 3;  // 8-column pieces (N % 8 == 0, R % 16 == 0): one 16-byte BF16 store each
-  const bool two_shot = p.world > kPeerOneShotMaxRanks;
-  if (!two_shot || p.rank == owner) {
-    bool ok = true;
-    if (threadIdx.x < p.world && threadIdx.x != p.rank)
-      ok = peer_wait_flag(peer_flags(own) + threadIdx.x * kPeerSlots + j, e);
-    if (!__syncthreads_and(ok)) return;
-    for (int i = threadIdx.x; i < p.M * w8; i += blockDim.x) {
-      const int m = i / w8;
-      const int64_t o = static_cast<int64_t>(m) * p.N + n0 + 8 * (i - m * w8);
-      const float* src0 = peer_inbox(own, p.capacity, parity, 0) + o;
-      float4 a = ld_volatile_f4(src0), b = ld_volatile_f4(src0 + 4);
+  if ((w & 3) == 0) {
+    const int wq = w >> 2;
+    for (int i = threadIdx.x; i < p.M * wq; i += blockDim.x) {
+      const int m = i / wq;
+      const int64_t o = static_cast<int64_t>(m) * p.N + n0 + 4 * (i - m * wq);
+      float4 s = ld_volatile_f4(peer_inbox(own, p.capacity, parity, 0) + o);
       for (int r = 1; r < p.world; ++r) {
-        const float* src = peer_inbox(own, p.capacity, parity, r) + o;
-        const float4 x = ld_volatile_f4(src), y = ld_volatile_f4(src + 4);
-        a.x = __fadd_rn(a.x, x.x);
-        a.y = __fadd_rn(a.y, x.y);
-        a.z = __fadd_rn(a.z, x.z);
-        a.w = __fadd_rn(a.w, x.w);
-        b.x = __fadd_rn(b.x, y.x);
-        b.y = __fadd_rn(b.y, y.y);
-        b.z = __fadd_rn(b.z, y.z);
-        b.w = __fadd_rn(b.w, y.w);
+        const float4 v = ld_volatile_f4(peer_inbox(own, p.capacity, parity, r) + o);
+        s.x = __fadd_rn(s.x, v.x);
+        s.y = __fadd_rn(s.y, v.y);
+        s.z = __fadd_rn(s.z, v.z);
+        s.w = __fadd_rn(s.w, v.w);
       }
-      __nv_bfloat162 h[4] = {__floats2bfloat162_rn(a.x, a.y), __floats2bfloat162_rn(a.z, a.w),
-                             __floats2bfloat162_rn(b.x, b.y), __floats2bfloat162_rn(b.z, b.w)};
-      const uint4 v = *reinterpret_cast<const uint4*>(h);
-      *reinterpret_cast<uint4*>(p.out + o) = v;
-      if (two_shot)
-        for (int k = 1; k < p.world; ++k) {  // every other rank, starting after this one
-          const int r = (p.rank + k) % p.world;
-          *reinterpret_cast<uint4*>(peer_result(p.bufs[r], p.capacity, parity) + o) = v;
-        }
+      __nv_bfloat162* d = reinterpret_cast<__nv_bfloat162*>(p.out + o);
+      d[0] = __floats2bfloat162_rn(s.x, s.y);
+      d[1] = __floats2bfloat162_rn(s.z, s.w);
     }
-    if (!two_shot) return;
-    // every thread's stores before one thread's system-scope release of done[j]
-    __syncthreads();
-    if (threadIdx.x == 0)
-      for (int r = 0; r < p.world; ++r)
-        if (r != p.rank) st_release_sys(peer_done(p.bufs[r]) + j, e);
   } else {
-    bool ok = true;
-    if (threadIdx.x == 0) ok = peer_wait_flag(peer_done(own) + j, e);
-    if (!__syncthreads_and(ok)) return;
-    const __nv_bfloat16* res = peer_result(own, p.capacity, parity);
-    for (int i = threadIdx.x; i < p.M * w8; i += blockDim.x) {
-      const int m = i / w8;
-      const int64_t o = static_cast<int64_t>(m) * p.N + n0 + 8 * (i - m * w8);
-      uint4 v;
-      asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
-                   : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                   : "l"(res + o));
-      *reinterpret_cast<uint4*>(p.out + o) = v;
+    for (int i = threadIdx.x; i < p.M * w; i += blockDim.x) {
+      const int m = i / w;
+      const int64_t o = static_cast<int64_t>(m) * p.N + n0 + (i - m * w);
+      float s = ld_volatile_f(peer_inbox(own, p.capacity, parity, 0) + o);
+      for (int r = 1; r < p.world; ++r) s = __fadd_rn(s, ld_volatile_f(peer_inbox(own, p.capacity, parity, r) + o));
+      p.out[o] = __float2bfloat16_rn(s);
     }
   }
 }
 
-int64_t peer_buffer_data_bytes(int64_t capacity) { return capacity * 4 * (1 + 2 * kPeerMaxRanks) + capacity * 2 * 2; }
+int64_t peer_buffer_data_bytes(int64_t capacity) { return capacity * 4 * (1 + 2 * kPeerMaxRanks); }
 
 int launch_peer_allreduce_bf16(void* const* bufs, int rank, int world, void* out, int64_t count, int64_t capacity,
                                cudaStream_t stream) {

@@ -5,12 +5,9 @@
 //   header  [NV4_PEER_HEADER_BYTES]
 //             flag[sender][slot]  uint32, kPeerMaxRanks x kPeerSlots
 //             epoch[slot]         uint32, kPeerSlots (this rank's call count)
-//             done[slot]          uint32, kPeerSlots (fused form: the tile's
-//                                 owner published its BF16 sum here)
 //   partial [capacity] FP32       this rank's partial (two-kernel path)
 //   inbox   [2][kPeerMaxRanks][capacity] FP32: slot (parity, sender) holds that
 //           sender's partial of a call with epoch parity `parity`
-//   result  [2][capacity] BF16    fused form: the summed tiles other ranks own
 //
 // Epochs: every call advances all kPeerSlots counters by one (a kernel's CTA s
 // advances slot s, its CTA 0 the slots beyond its grid), so all slots hold the
@@ -32,11 +29,7 @@ constexpr int kPeerMaxRanks = 8;
 constexpr int kPeerSlots = 256;
 constexpr int kPeerHeaderBytes = NV4_PEER_HEADER_BYTES;
 constexpr int kErrTimeoutPeer = 5;  // a peer rank did not reach the same call in time
-// The fused row-parallel sum is one-shot (every rank receives every tile) up to
-// this many ranks and two-shot (each tile summed on one owner rank) above it:
-// at 2 ranks the second hand-off costs more than the data it saves.
-constexpr int kPeerOneShotMaxRanks = 2;
-static_assert((kPeerMaxRanks + 2) * kPeerSlots * 4 <= kPeerHeaderBytes, "peer header too small");
+static_assert((kPeerMaxRanks + 1) * kPeerSlots * 4 <= kPeerHeaderBytes, "peer header too small");
 
 __device__ __forceinline__ uint32_t* peer_flags(uint8_t* buf) { return reinterpret_cast<uint32_t*>(buf); }
 __device__ __forceinline__ uint32_t* peer_epochs(uint8_t* buf) {
@@ -47,13 +40,6 @@ __device__ __forceinline__ float* peer_partial(uint8_t* buf) {
 }
 __device__ __forceinline__ float* peer_inbox(uint8_t* buf, int64_t capacity, int parity, int sender) {
   return peer_partial(buf) + capacity * (1 + parity * kPeerMaxRanks + sender);
-}
-__device__ __forceinline__ uint32_t* peer_done(uint8_t* buf) {
-  return reinterpret_cast<uint32_t*>(buf) + (kPeerMaxRanks + 1) * kPeerSlots;
-}
-__device__ __forceinline__ __nv_bfloat16* peer_result(uint8_t* buf, int64_t capacity, int parity) {
-  return reinterpret_cast<__nv_bfloat16*>(peer_partial(buf) + capacity * (1 + 2 * kPeerMaxRanks)) +
-         capacity * parity;
 }
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {

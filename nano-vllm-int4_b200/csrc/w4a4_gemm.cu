@@ -645,20 +645,16 @@ __global__ void __launch_bounds__(32 * (kProducerWarps + (KS == 1 && TPW == MT ?
     }
   }
   if (p.peer_world) {
-    // The staged tile goes out in 16-byte stores (whole token rows of the
-    // CTA's R columns): to every rank's inbox (one-shot, each CTA starting at
-    // a different rank), or, above kPeerOneShotMaxRanks ranks, only to the
-    // inbox of its owner, rank blockIdx.x % world (the reduce-scatter half of
-    // the two-shot sum).  After every consumer's stores, one thread's
-    // system-scope release of this CTA's flag on each receiving peer (released
-    // on error too, so that the peers do not wait out their limit; the error
-    // word marks the call as failed).
+    // The staged tile goes to every rank's inbox in 16-byte stores (whole
+    // token rows of the CTA's R columns; each CTA starts with a different
+    // rank, spreading the NVLink traffic), then, after every consumer's
+    // stores, one thread's system-scope release of this CTA's flag on each
+    // peer (released on error too, so that the peers do not wait out their
+    // limit; the error word marks the call as failed).
     named_barrier_sync(1, cthreads);
-    const bool two_shot = p.peer_world > kPeerOneShotMaxRanks;
-    const int owner = static_cast<int>(blockIdx.x) % p.peer_world;
     const int wq = min(R, p.N - n0) >> 2, rows = min(MP, p.M - m0);
-    for (int j = 0; j < (two_shot ? 1 : p.peer_world); ++j) {
-      const int r = two_shot ? owner : (static_cast<int>(blockIdx.x) + j) % p.peer_world;
+    for (int j = 0; j < p.peer_world; ++j) {
+      const int r = (static_cast<int>(blockIdx.x) + j) % p.peer_world;
       float* dst = peer_inbox(p.peer_bufs[r], p.peer_capacity, peer_parity, p.peer_rank);
       for (int i = ct; i < rows * wq; i += cthreads) {
         const int t = i / wq, c = i - t * wq;
@@ -670,8 +666,7 @@ __global__ void __launch_bounds__(32 * (kProducerWarps + (KS == 1 && TPW == MT ?
     if (ct == 0) {
       const uint32_t e = static_cast<uint32_t>(fast_g[G + 1]);
       for (int r = 0; r < p.peer_world; ++r)
-        if (r != p.peer_rank && (!two_shot || r == owner))
-          st_release_sys(peer_flags(p.peer_bufs[r]) + p.peer_rank * kPeerSlots + blockIdx.x, e);
+        if (r != p.peer_rank) st_release_sys(peer_flags(p.peer_bufs[r]) + p.peer_rank * kPeerSlots + blockIdx.x, e);
     }
   }
 }
