@@ -742,8 +742,8 @@ int plan_w4a4_stream(int64_t m, int64_t n, int64_t k, bool wg, int sms, bool pee
   slabs = std::max(1, slabs);
   // Narrow layers (up to 4 slabs per CTA): split K over 4 warps per slab, and
   // with 32 tokens and at most 2 slabs also split the token tiles over two
-  // warps (16 consumer warps).  5-8 slabs take 4-slab CTAs (more CTAs than
-  // SMs) rather than a 2-way K split.  Wider ones: one warp per slab.
+  // warps (16 consumer warps).  Wider ones: one warp per slab (see below for
+  // 5-8 slabs).
   //
   // Ring rule.  A producer warp reuses a slot after waiting on its empty
   // barrier by phase parity, which is only sound if the slot's previous phase
@@ -752,7 +752,12 @@ int plan_w4a4_stream(int64_t m, int64_t n, int64_t k, bool wg, int sms, bool pee
   // any order, so the ring must hold KS + kProducerWarps stages (or all of K):
   // with fewer, a producer can pass the wait one phase early and a TMA copy
   // can overwrite a slot still being read.  Fewer slabs per CTA until it fits.
-  if (slabs > 4 && slabs <= 8) slabs = 4;
+  // With more than 8 tokens, 5-8 slab CTAs keep their slabs with one warp per
+  // slab and the token tiles split over two warps (measured: 16 us against
+  // 22 us for 4-slab CTAs in two waves at N = 12288, K = 4096, M = 32); with
+  // up to 8 tokens there are no token tiles to split, and 4-slab CTAs with the
+  // 4-way K split are faster.
+  if (slabs > 4 && slabs <= 8 && MT < 2) slabs = 4;
   // Peer mode stores one flag per CTA, so the grid must fit kPeerSlots: start
   // from enough slabs per CTA for that (the ring rule may still lower it).
   if (peer) slabs = std::max<int>(slabs, static_cast<int>(std::min<int64_t>(kMaxWideSlabs, (total_slabs + kPeerSlots - 1) / kPeerSlots)));

@@ -138,8 +138,8 @@ def test_extreme_scales(cuda_device):
                                    (17, 96, 512), (33, 136, 4096), (100, 64, 2048), (5, 24, 384),
                                    (128, 256, 4096), (300, 512, 1024), (1024, 384, 12288),
                                    (16, 30720, 1024), (3, 38016, 256), (24, 1000, 640),
-                                   # 5-8 slabs per SM go to 4-slab CTAs (more CTAs than SMs), and
-                                   # 9-16 tokens with a K split of 4
+                                   # 5-8 slabs per SM: one warp per slab with split token tiles
+                                   # above 8 tokens, 4-slab CTAs (more CTAs than SMs) up to 8
                                    (32, 12288, 4096), (1, 12288, 4096), (12, 12288, 4096), (16, 4096, 4096)])
 def test_i8_activation_gemm_exact(cuda_device, m, n, k, grouped, path):
     """nv4_w4a4_gemm_i8 (the path W4A4Linear uses) equals the oracle bit for bit
