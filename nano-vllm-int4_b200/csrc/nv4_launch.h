@@ -74,8 +74,12 @@ int launch_w4a16_gemm(const void* x, const void* qweight, const void* qzeros, co
                       int64_t m, int64_t n, int64_t k, void* workspace, int64_t workspace_bytes, cudaStream_t stream);
 int64_t w4a16_workspace_bytes(int64_t m, int64_t n, int64_t k);
 // W4A16 on tcgen05 (prefill shapes); NV4_ERR_UNSUPPORTED for shapes it does not take.
+// K is split (FP32 partials in `workspace`) when its plan asks for it and the
+// workspace holds w4a16_tc_workspace_bytes; otherwise it is not.
 int launch_w4a16_tc_gemm(const void* x, const void* qweight, const void* qzeros, const void* scales, void* out,
-                         int64_t m, int64_t n, int64_t k, cudaStream_t stream);
+                         int64_t m, int64_t n, int64_t k, void* workspace, int64_t workspace_bytes,
+                         cudaStream_t stream);
+int64_t w4a16_tc_workspace_bytes(int64_t m, int64_t n, int64_t k);
 // Same as launch_w4a16_gemm with the library's static scratch as workspace.
 int launch_w4a16_gemm_static(const void* x, const void* qweight, const void* qzeros, const void* scales, void* out,
                              int64_t m, int64_t n, int64_t k, cudaStream_t stream);

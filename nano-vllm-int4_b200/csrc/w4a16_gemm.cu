@@ -566,11 +566,13 @@ int64_t w4a16_workspace_bytes(int64_t m, int64_t n, int64_t k) {
   if (sms <= 0) return 0;
   W4A16StreamPlan sp;
   if (plan_w4a16_stream(m, n, k, sms, &sp)) return 0;
+  if (m > 32) return std::max(w4a16_tc_workspace_bytes(m, n, k), w4a16_mma_workspace_bytes(m, n, k, sms));
   return w4a16_mma_workspace_bytes(m, n, k, sms);
 }
 
-// Up to 32 tokens: Kernel D1 (no workspace); more: Kernel D2 (tcgen05); shapes
-// neither takes: the mma.sync kernel.
+// Up to 32 tokens: Kernel D1 (no workspace); more: Kernel D2 (tcgen05, split-K
+// partials in the workspace when its plan splits); shapes neither takes: the
+// mma.sync kernel.
 int launch_w4a16_gemm(const void* x, const void* qweight, const void* qzeros, const void* scales, void* out,
                       int64_t m, int64_t n, int64_t k, void* workspace, int64_t workspace_bytes, cudaStream_t stream) {
   const int sms = device_sm_count();
@@ -579,7 +581,7 @@ int launch_w4a16_gemm(const void* x, const void* qweight, const void* qzeros, co
   if (plan_w4a16_stream(m, n, k, sms, &sp) && (reinterpret_cast<uintptr_t>(qweight) & 15) == 0)
     return launch_w4a16_stream(x, qweight, qzeros, scales, out, m, n, k, sp, stream);
   if (m > 32) {
-    const int rc = launch_w4a16_tc_gemm(x, qweight, qzeros, scales, out, m, n, k, stream);
+    const int rc = launch_w4a16_tc_gemm(x, qweight, qzeros, scales, out, m, n, k, workspace, workspace_bytes, stream);
     if (rc != NV4_ERR_UNSUPPORTED) return rc;
   }
   return launch_w4a16_mma(x, qweight, qzeros, scales, out, m, n, k, workspace, workspace_bytes, stream);

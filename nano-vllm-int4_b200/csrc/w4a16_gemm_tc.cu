@@ -4,9 +4,13 @@
 // out[m, n] = sum_k x[m, k] * Wdq[k, n] with the reference's dequantisation
 // (nanovllm/layers/linear_w4a16.py:45-55): Wdq = bf16((w - z - 1) * bf16(scale)),
 // computed as bf16(128 + w) - bf16(129 + z) (exact) times the BF16-rounded FP16
-// scale (one BF16 rounding).  FP32 accumulation over all of K in tensor memory,
-// one BF16 rounding of the result; no split-K.  (The reference adds BF16-rounded
-// split-K partials with BF16 atomics, so results agree within a tolerance.)
+// scale (one BF16 rounding).  FP32 accumulation in tensor memory.  When the
+// tiles do not fill the SMs (few weight-column blocks, up to a few hundred
+// tokens), K is split into up to 8 slices: each slice's FP32 partial tile goes
+// to a workspace and a second kernel adds the slices in slice order (fixed
+// order, deterministic) and rounds to BF16 once; otherwise one BF16 rounding of
+// the full-K accumulator.  (The reference adds BF16-rounded split-K partials
+// with BF16 atomics, so results agree within a tolerance.)
 //
 // The MMA computes D[n, t] = A[n, k] * B[t, k]^T with
 //   A = dequantised weights: M = 128 weight columns n, held in tensor memory
@@ -14,8 +18,8 @@
 //       the widened weights never touch shared memory;
 //   B = activations: N = BN tokens, BF16 K-major with the 128-byte swizzle,
 //       exactly as TMA lands them.
-// Persistent: one CTA per SM walks tiles of 128 weight columns x BN tokens
-// over all of K, 64 K per pipeline chunk:
+// Persistent: one CTA per SM walks work units -- a tile of 128 weight columns x
+// BN tokens over one K slice -- 64 K per pipeline chunk:
 //   warp 0      TMA producer: per chunk, the x tile [BN x 64 k], the packed
 //               weight tile [8 rows of k/8 x 128 columns] and the chunk's group
 //               row of scales [128] and zero points [16 words] into an S-slot
@@ -42,13 +46,34 @@
 
 namespace nv4 {
 
+constexpr int kD2Chunk = 64;          // K per pipeline chunk
+
 struct W4A16TcArgs {
-  uint16_t* out;           // bf16 [M, N]
+  uint16_t* out;           // bf16 [M, N] (one K slice)
+  float* partial;          // fp32 [splits, M, N] (more than one K slice)
   int M, N, K;
-  int tiles_m, tiles;      // token blocks; tiles (token blocks fastest)
+  int tiles_m, splits;     // token blocks; K slices
+  int units;               // column blocks x splits x token blocks (token blocks fastest, then slices)
 };
 
-constexpr int kD2Chunk = 64;          // K per pipeline chunk
+// One work unit: column block, token block, K slice and its chunk range
+// [cb, ce) (slices differ by at most one chunk).
+struct D2Unit {
+  int nb, mb, split, cb, ce;
+};
+
+__device__ __forceinline__ D2Unit d2_unit(const W4A16TcArgs& p, int t) {
+  D2Unit u;
+  u.mb = t % p.tiles_m;
+  const int r = t / p.tiles_m;
+  u.split = r % p.splits;
+  u.nb = r / p.splits;
+  const int kct = p.K / kD2Chunk;
+  u.cb = (u.split * kct) / p.splits;
+  u.ce = ((u.split + 1) * kct) / p.splits;
+  return u;
+}
+
 constexpr int kD2DequantWarps = 8;    // two per TMEM lane quarter (alternate chunks)
 constexpr int kD2EpiWarps = 16;       // four per lane quarter
 constexpr int kD2FirstEpiWarp = 2 + kD2DequantWarps;
@@ -163,11 +188,14 @@ __global__ void __launch_bounds__(kD2Threads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int KC = p.K / kD2Chunk;  // chunks per tile
-  const int my_tiles = p.tiles > static_cast<int>(blockIdx.x)
-                           ? (p.tiles - static_cast<int>(blockIdx.x) + gridDim.x - 1) / gridDim.x : 0;
-  const int total = my_tiles * KC;
-  auto tile_of = [&](int i) { return static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x); };
+  const int my_units = p.units > static_cast<int>(blockIdx.x)
+                           ? (p.units - static_cast<int>(blockIdx.x) + gridDim.x - 1) / gridDim.x : 0;
+  auto unit_of = [&](int i) { return d2_unit(p, static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x)); };
+  int total = 0;  // pipeline chunks of this CTA (every unit has at least one)
+  for (int i = 0; i < my_units; ++i) {
+    const D2Unit u = unit_of(i);
+    total += u.ce - u.cb;
+  }
   grid_dependents_launch();
 
   if (threadIdx.x == 0) {
@@ -201,29 +229,42 @@ __global__ void __launch_bounds__(kD2Threads, 1)
       tma_prefetch_desc(&tmap_sc);
       tma_prefetch_desc(&tmap_qz);
       const uint64_t wpol = policy_evict_first();
-      auto load_w = [&](int c) {  // first of a slot's copies: expects all of them
-        const int s = c % S, t = tile_of(c / KC), kc = c % KC, n0 = (t / p.tiles_m) * 128;
+      // (unit, chunk) walk over this CTA's units in order
+      struct Walk {
+        D2Unit u;
+        int i, kc;
+      };
+      auto walk_start = [&]() { Walk w{unit_of(0), 0, 0}; w.kc = w.u.cb; return w; };
+      auto walk_step = [&](Walk& w) {
+        if (++w.kc == w.u.ce && ++w.i < my_units) {
+          w.u = unit_of(w.i);
+          w.kc = w.u.cb;
+        }
+      };
+      auto load_w = [&](int c, const Walk& w) {  // first of a slot's copies: expects all of them
+        const int s = c % S, n0 = w.u.nb * 128;
         uint8_t* st = smem + s * L::kStage;
         mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(L::kBytes));
-        tma_load_2d_hint(st + L::kX, &tmap_qw, &full[s], n0, kc * 8, wpol);
-        tma_load_2d(st + L::kX + L::kW, &tmap_sc, &full[s], n0, (kc * kD2Chunk) / 128);
-        tma_load_2d(st + L::kX + L::kW + L::kS, &tmap_qz, &full[s], n0 / 8, (kc * kD2Chunk) / 128);
+        tma_load_2d_hint(st + L::kX, &tmap_qw, &full[s], n0, w.kc * 8, wpol);
+        tma_load_2d(st + L::kX + L::kW, &tmap_sc, &full[s], n0, (w.kc * kD2Chunk) / 128);
+        tma_load_2d(st + L::kX + L::kW + L::kS, &tmap_qz, &full[s], n0 / 8, (w.kc * kD2Chunk) / 128);
       };
-      auto load_x = [&](int c) {
-        const int s = c % S, t = tile_of(c / KC), kc = c % KC;
-        tma_load_2d(smem + s * L::kStage, &tmap_x, &full[s], kc * kD2Chunk, (t % p.tiles_m) * BN);
+      auto load_x = [&](int c, const Walk& w) {
+        tma_load_2d(smem + (c % S) * L::kStage, &tmap_x, &full[c % S], w.kc * kD2Chunk, w.u.mb * BN);
       };
       // the first chunks' weights stream while the preceding kernel finishes
       const int first = min(S, total);
-      for (int c = 0; c < first; ++c) load_w(c);
+      Walk wk = walk_start();
+      for (int c = 0; c < first; ++c, walk_step(wk)) load_w(c, wk);
       grid_dependency_wait();  // the activations come from the preceding kernel
-      for (int c = 0; c < first; ++c) load_x(c);
+      Walk wx = walk_start();
+      for (int c = 0; c < first; ++c, walk_step(wx)) load_x(c, wx);
       int issued = first;
-      for (int c = first; c < total; ++c) {
+      for (int c = first; c < total; ++c, walk_step(wk)) {
         const int s = c % S;
         if (!mbar_wait(&consumed[s], ((c / S) - 1) & 1, kErrTimeoutEmpty)) break;
-        load_w(c);
-        load_x(c);
+        load_w(c, wk);
+        load_x(c, wk);
         issued = c + 1;
       }
       // every copy issued must land before the CTA may exit
@@ -234,21 +275,26 @@ __global__ void __launch_bounds__(kD2Threads, 1)
     // ---------------- MMA issuer: 4 x (M=128 columns, N=BN tokens, K=16) per chunk
     if (lane == 0) {
       const uint32_t stage_base = smem_u32(smem);
-      for (int c = 0; c < total && ok; ++c) {
-        const int s = c % S, ti = c / KC, kc = c % KC, b = ti % NA;
-        if (kc == 0) ok = mbar_wait(&tfree[b], (ti / NA) & 1, kErrTimeoutMma);
-        // afull[s] implies full[s]: the dequant warps waited for both copies
-        ok = ok && mbar_wait(&afull[s], (c / S) & 1, kErrTimeoutMma);
-        if (!ok) break;
-        tc_fence_after();
-        const uint32_t x_addr = stage_base + s * L::kStage;
-        const uint32_t a_tmem = tmem + kD2ACol + 32u * s;
+      int c = 0;
+      for (int ui = 0; ui < my_units && ok; ++ui) {
+        const D2Unit u = unit_of(ui);
+        const int b = ui % NA;
+        for (int kc = u.cb; kc < u.ce; ++kc, ++c) {
+          const int s = c % S;
+          if (kc == u.cb) ok = mbar_wait(&tfree[b], (ui / NA) & 1, kErrTimeoutMma);
+          // afull[s] implies full[s]: the dequant warps waited for both copies
+          ok = ok && mbar_wait(&afull[s], (c / S) & 1, kErrTimeoutMma);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t x_addr = stage_base + s * L::kStage;
+          const uint32_t a_tmem = tmem + kD2ACol + 32u * s;
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          umma_bf16_ts(tmem + b * BN, a_tmem + 8u * j, umma_desc_sw128(x_addr + 32 * j), IDESC,
-                       (kc > 0 || j > 0) ? 1u : 0u);
-        umma_commit(&consumed[s]);
-        if (kc == KC - 1) umma_commit(&tfull[b]);
+          for (int j = 0; j < 4; ++j)
+            umma_bf16_ts(tmem + b * BN, a_tmem + 8u * j, umma_desc_sw128(x_addr + 32 * j), IDESC,
+                         (kc > u.cb || j > 0) ? 1u : 0u);
+          umma_commit(&consumed[s]);
+          if (kc == u.ce - 1) umma_commit(&tfull[b]);
+        }
       }
       // all issued MMAs must finish before the TMEM is released
       umma_commit(done_bar);
@@ -287,7 +333,8 @@ __global__ void __launch_bounds__(kD2Threads, 1)
       if (lane == 0) mbar_arrive(&afull[s]);
     }
   } else {
-    // ---------------- epilogue: thread = weight column, BN/4 token columns
+    // ---------------- epilogue: thread = weight column, BN/4 token columns;
+    // BF16 out (one K slice) or the slice's FP32 partial
     constexpr int kCols = BN / 4;
     const int ew = warp - kD2FirstEpiWarp;
     const int quarter = warp & 3;
@@ -296,25 +343,35 @@ __global__ void __launch_bounds__(kD2Threads, 1)
     __syncwarp();
     if (lane == 0)
       for (int b = 0; b < NA; ++b) mbar_arrive(&tfree[b]);  // every accumulator starts free
-    for (int ti = 0; ti < my_tiles && ok; ++ti) {
-      const int b = ti % NA;
-      ok = mbar_wait(&tfull[b], (ti / NA) & 1, kErrTimeoutMma);
+    for (int ui = 0; ui < my_units && ok; ++ui) {
+      const int b = ui % NA;
+      ok = mbar_wait(&tfull[b], (ui / NA) & 1, kErrTimeoutMma);
       if (!ok) break;
       tc_fence_after();
-      const int t = tile_of(ti);
-      const int n = (t / p.tiles_m) * 128 + quarter * 32 + lane;
-      const int m0 = (t % p.tiles_m) * BN + c0;
+      const D2Unit u = unit_of(ui);
+      const int n = u.nb * 128 + quarter * 32 + lane;
+      const int m0 = u.mb * BN + c0;
+      float* part = p.partial + static_cast<size_t>(u.split) * p.M * p.N;
 #pragma unroll
       for (int c = 0; c < kCols; c += 32) {
         uint32_t v[32];
         tmem_ld32(taddr + b * BN + c, v);
         tmem_wait_ld();
         if (n < p.N) {
+          if (p.splits == 1) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int m = m0 + c + j;
-            if (m < p.M)
-              p.out[static_cast<size_t>(m) * p.N + n] = __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[j])));
+            for (int j = 0; j < 32; ++j) {
+              const int m = m0 + c + j;
+              if (m < p.M)
+                p.out[static_cast<size_t>(m) * p.N + n] =
+                    __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[j])));
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int m = m0 + c + j;
+              if (m < p.M) part[static_cast<size_t>(m) * p.N + n] = __uint_as_float(v[j]);
+            }
           }
         }
       }
@@ -331,6 +388,38 @@ __global__ void __launch_bounds__(kD2Threads, 1)
   }
 }
 
+// Split-K sum: out = bf16(partial[0] + partial[1] + ...), slices added in
+// order, four outputs per thread.
+constexpr int kD2MaxSplits = 8;
+
+__global__ void __launch_bounds__(256) w4a16_split_sum_kernel(const float* __restrict__ partial,
+                                                              uint16_t* __restrict__ out, int64_t count4,
+                                                              int64_t slice4, int splits) {
+  grid_dependency_wait();  // the partials come from the preceding GEMM
+  grid_dependents_launch();
+  const float4* src = reinterpret_cast<const float4*>(partial);
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count4;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float4 v[kD2MaxSplits];
+#pragma unroll
+    for (int s = 0; s < kD2MaxSplits; ++s)  // every load before the sum
+      if (s < splits) v[s] = __ldcs(src + s * slice4 + i);
+    float4 a = v[0];
+#pragma unroll
+    for (int s = 1; s < kD2MaxSplits; ++s)
+      if (s < splits) {
+        a.x = __fadd_rn(a.x, v[s].x);
+        a.y = __fadd_rn(a.y, v[s].y);
+        a.z = __fadd_rn(a.z, v[s].z);
+        a.w = __fadd_rn(a.w, v[s].w);
+      }
+    uint2 o;
+    o.x = __bfloat16_as_ushort(__float2bfloat16_rn(a.x)) | (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(a.y))) << 16);
+    o.y = __bfloat16_as_ushort(__float2bfloat16_rn(a.z)) | (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(a.w))) << 16);
+    reinterpret_cast<uint2*>(out)[i] = o;
+  }
+}
+
 // ------------------------------------------------------------ host side
 template <int BN>
 static int launch_w4a16_tc_t(const CUtensorMap* maps, const W4A16TcArgs& a, int sms, cudaStream_t stream) {
@@ -339,22 +428,65 @@ static int launch_w4a16_tc_t(const CUtensorMap* maps, const W4A16TcArgs& a, int 
   const int smem = D2Layout<BN>::kTotal + 1024;
   const int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem, done);
   if (rc != NV4_OK) return rc;
-  const dim3 grid(static_cast<unsigned>(std::min<int64_t>(a.tiles, sms)));
+  const dim3 grid(static_cast<unsigned>(std::min<int64_t>(a.units, sms)));
   return launch_kernel(kern, grid, dim3(kD2Threads), smem, stream, true, maps[0], maps[1], maps[2], maps[3], a);
 }
 
-// Token tiles of 256 when there are enough tokens to fill them, else 128.
+// Token tile (256 when there are more than 128 tokens, else 128) and K split.
+// The split count comes from a cost model: a 64-K chunk takes ~0.55 us per SM
+// whatever the token tile (the dequantisation sets the rate), units run in
+// rounds of `sms`, and a split adds its FP32 partials' write and read (at
+// ~6 TB/s) plus ~2 us for the sum kernel; a split count is taken only when it
+// is at least 5% faster than the best fewer splits.
+struct D2Plan {
+  int bn, splits;
+};
+
+static D2Plan plan_w4a16_tc(int64_t m, int64_t n, int64_t k, int sms) {
+  constexpr double kChunkUs = 0.55, kSumUs = 2.0, kBytesPerUs = 6.0e6;
+  D2Plan pl;
+  pl.bn = m > 128 ? 256 : 128;
+  pl.splits = 1;
+  const int64_t base = ((n + 127) / 128) * ((m + pl.bn - 1) / pl.bn), kct = k / kD2Chunk;
+  double best = 0.0;
+  for (int s = 1; s <= kD2MaxSplits && s <= kct; ++s) {
+    const int64_t rounds = (base * s + sms - 1) / sms, span = (kct + s - 1) / s;
+    double t = static_cast<double>(rounds * span) * kChunkUs;
+    if (s > 1) t += kSumUs + static_cast<double>(s) * static_cast<double>(m * n) * 8.0 / kBytesPerUs;
+    if (s == 1 || t < 0.95 * best) {
+      best = t;
+      pl.splits = s;
+    }
+  }
+  return pl;
+}
+
+// Workspace the split plan of a shape wants (0: no split).
+int64_t w4a16_tc_workspace_bytes(int64_t m, int64_t n, int64_t k) {
+  const int sms = device_sm_count();
+  if (sms <= 0 || m < 1 || n < 32 || k < 128) return 0;
+  const D2Plan pl = plan_w4a16_tc(m, n, k, sms);
+  return pl.splits > 1 ? pl.splits * m * n * static_cast<int64_t>(sizeof(float)) : 0;
+}
+
 // Shapes outside the kernel's alignment rules return NV4_ERR_UNSUPPORTED (the
-// caller then takes the mma.sync kernel).
+// caller then takes the mma.sync kernel).  Without a workspace of the plan's
+// size (or with one not 16-byte aligned, or `out` not 8-byte aligned) K is
+// not split.
 int launch_w4a16_tc_gemm(const void* x, const void* qweight, const void* qzeros, const void* scales, void* out,
-                         int64_t m, int64_t n, int64_t k, cudaStream_t stream) {
+                         int64_t m, int64_t n, int64_t k, void* workspace, int64_t workspace_bytes,
+                         cudaStream_t stream) {
   if (m < 1 || n < 32 || n % 32 || k < 128 || k % 128 || (reinterpret_cast<uintptr_t>(x) & 15) ||
       (reinterpret_cast<uintptr_t>(qweight) & 15) || (reinterpret_cast<uintptr_t>(qzeros) & 15) ||
       (reinterpret_cast<uintptr_t>(scales) & 15) || m > (int64_t(1) << 30) || n > (int64_t(1) << 30))
     return NV4_ERR_UNSUPPORTED;
   const int sms = device_sm_count();
   if (sms <= 0) return NV4_ERR_CUDA;
-  const int bn = m > 128 ? 256 : 128;
+  D2Plan pl = plan_w4a16_tc(m, n, k, sms);
+  if (pl.splits > 1 && (workspace == nullptr || workspace_bytes < pl.splits * m * n * static_cast<int64_t>(sizeof(float)) ||
+                        (reinterpret_cast<uintptr_t>(workspace) & 15) || (reinterpret_cast<uintptr_t>(out) & 7)))
+    pl.splits = 1;
+  const int bn = pl.bn;
   CUtensorMap maps[4];
   memset(maps, 0, sizeof(maps));
   const bool okm = make_tensor_map_2d(&maps[0], CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, x, static_cast<uint64_t>(m),
@@ -369,14 +501,21 @@ int launch_w4a16_tc_gemm(const void* x, const void* qweight, const void* qzeros,
   if (!okm) return NV4_ERR_CUDA;
   W4A16TcArgs a;
   a.out = static_cast<uint16_t*>(out);
+  a.partial = pl.splits > 1 ? static_cast<float*>(workspace) : nullptr;
   a.M = static_cast<int>(m);
   a.N = static_cast<int>(n);
   a.K = static_cast<int>(k);
   a.tiles_m = static_cast<int>((m + bn - 1) / bn);
-  const int64_t tiles = ((n + 127) / 128) * a.tiles_m;
-  if (tiles > (int64_t(1) << 30)) return NV4_ERR_UNSUPPORTED;
-  a.tiles = static_cast<int>(tiles);
-  return bn == 256 ? launch_w4a16_tc_t<256>(maps, a, sms, stream) : launch_w4a16_tc_t<128>(maps, a, sms, stream);
+  a.splits = pl.splits;
+  const int64_t units = ((n + 127) / 128) * a.tiles_m * pl.splits;
+  if (units > (int64_t(1) << 30)) return NV4_ERR_UNSUPPORTED;
+  a.units = static_cast<int>(units);
+  const int rc = bn == 256 ? launch_w4a16_tc_t<256>(maps, a, sms, stream) : launch_w4a16_tc_t<128>(maps, a, sms, stream);
+  if (rc != NV4_OK || pl.splits == 1) return rc;
+  const int64_t count4 = m * n / 4;  // n is a multiple of 32
+  const int blocks = static_cast<int>(std::min<int64_t>((count4 + 255) / 256, 2 * static_cast<int64_t>(sms)));
+  return launch_kernel(w4a16_split_sum_kernel, dim3(blocks), dim3(256), 0, stream, true,
+                       static_cast<const float*>(workspace), static_cast<uint16_t*>(out), count4, count4, pl.splits);
 }
 
 }  // namespace nv4

@@ -133,11 +133,14 @@ def test_w4a16_matches_oracle(cuda_device, n, k, m):
     assert rel_b < 1e-3, rel_b      # same BF16 rounding as the exact product, up to FP32 sums
 
 
-@pytest.mark.parametrize("m,n,k", [(33, 192, 512), (300, 320, 1024), (257, 4096, 12288), (2048, 24576, 4096)])
+@pytest.mark.parametrize("m,n,k", [(33, 192, 512), (300, 320, 1024), (257, 4096, 12288), (2048, 24576, 4096),
+                                   (128, 6144, 4096), (128, 4096, 12288)])
 def test_w4a16_prefill_tiles(cuda_device, m, n, k):
     """The tcgen05 W4A16 kernel (more than 32 tokens): ragged token and column
-    tiles (zero-filled TMA boxes past M and N, stores masked) and a full
-    config-3 prefill shape, on a sample of rows against the float64 oracle."""
+    tiles (zero-filled TMA boxes past M and N, stores masked), K split into 2-8
+    slices (uneven ones at 128 x 6144 x 4096) summed by the second kernel, and
+    an unsplit full config-3 prefill shape, on a sample of rows against the
+    float64 oracle."""
     qweight, qzeros, scales = synthetic.w4a16_weights(n, k, seed=7 * n + k)
     layer = W4A16Linear(k, n).to(cuda_device)
     with torch.no_grad():
@@ -155,6 +158,36 @@ def test_w4a16_prefill_tiles(cuda_device, m, n, k):
     assert rel < 4e-3, rel
     exp_bf16 = o.round_to_bf16(expected.astype(np.float32)).astype(np.float64)
     assert np.linalg.norm(got[rows] - exp_bf16) / np.linalg.norm(expected) < 1e-3
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 4096, 12288), (64, 6144, 4096)])
+def test_w4a16_split_k_without_workspace(cuda_device, m, n, k):
+    """A shape whose plan splits K: with the queried workspace the slices' FP32
+    partials are summed by the second kernel; without one the kernel runs
+    unsplit.  Both agree with the oracle and with each other up to FP32
+    summation order."""
+    ws_bytes = _native.w4a16_workspace_bytes(m, n, k, cuda_device)
+    assert ws_bytes >= 2 * m * n * 4  # the plan splits
+    qweight, qzeros, scales = synthetic.w4a16_weights(n, k, seed=3 * n + k)
+    qw, qz, sc = qweight.to(cuda_device), qzeros.to(cuda_device), scales.to(cuda_device)
+    x = synthetic.activations(m, k, seed=m + 11)
+    xd = x.to(cuda_device)
+    ws = torch.empty(ws_bytes // 4, dtype=torch.float32, device=cuda_device)
+    split = torch.empty(m, n, dtype=torch.bfloat16, device=cuda_device)
+    whole = torch.empty(m, n, dtype=torch.bfloat16, device=cuda_device)
+    _native.w4a16_gemm(xd, qw, qz, sc, split, 128, ws)
+    _native.w4a16_gemm(xd, qw, qz, sc, whole, 128, None)
+    torch.cuda.synchronize()
+    assert _native.device_error() == 0
+    rows = np.arange(0, m, 5)
+    expected = o.w4a16_gemm_f64(u16(x[rows]), qweight.numpy(), qzeros.numpy(), scales.numpy())
+    for got in (split, whole):
+        g = got.float().cpu().numpy().astype(np.float64)[rows]
+        assert np.linalg.norm(g - expected) / np.linalg.norm(expected) < 4e-3
+    # one BF16 rounding step apart, or FP32-summation noise near cancellations
+    diff = (split.float() - whole.float()).abs()
+    rms = whole.float().pow(2).mean().sqrt()
+    assert (diff <= whole.float().abs() * 2 ** -7 + 1e-3 * rms).all()
 
 
 def test_w4a16_large_m_and_graph(cuda_device):
