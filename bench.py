@@ -437,7 +437,8 @@ def measure_prefill(mods, device, stream, int8):
 
 
 def measure_w4a16(device, stream, peaks):
-    """Config 3: W4A16Linear at M in {1, 16, 128, 2048}.  Small M streams
+    """Config 3: W4A16Linear at M in {1, 16, 128, 2048}, plus 32 (the decode
+    batch of the end-to-end model).  Small M streams
     distinct weight copies (more than 256 MB in total, larger than L2)."""
     from nanovllm.layers.linear_w4a16 import W4A16Linear
     out = {}
@@ -457,7 +458,7 @@ def measure_w4a16(device, stream, peaks):
                 lin.scales.copy_((torch.randn(lin.scales.shape, device=device, generator=g).abs() * 0.02).half())
             mods.append(lin)
         row = {}
-        for m in (1, 16, 128, 2048):
+        for m in (1, 16, 32, 128, 2048):
             x = torch.randn(m, k, device=device, generator=g).bfloat16()
             use = mods if m <= 16 else mods[:2]
 

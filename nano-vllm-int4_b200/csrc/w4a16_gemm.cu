@@ -214,7 +214,7 @@ static int launch_w4a16_mma(const void* x, const void* qweight, const void* qzer
 }
 
 // ------------------------------------------------------------ Kernel D1: decode
-// W4A16 for up to 32 tokens: the weights are the streamed operand.  A CTA
+// W4A16 for up to 16 tokens: the weights are the streamed operand.  A CTA
 // owns 64 output columns and a K slice; the KS CTAs of one column block form
 // a thread-block cluster along K (split-K, the reference's SPLIT_K for small
 // M), and their FP32 partial tiles are summed through distributed shared
@@ -229,8 +229,12 @@ static int launch_w4a16_mma(const void* x, const void* qweight, const void* qzer
 //    the nibble pairs (j, j+4) that one shift and mask pull out of a packed
 //    word (a consistent K permutation of both operands leaves every dot
 //    product unchanged).
-//  * mma.sync m16n8k16 BF16 with tokens as M (16 per tile, up to two tiles)
-//    and weight columns as N: warp w owns columns 16w .. 16w+15.
+//  * mma.sync m16n8k16 BF16 with tokens as M (one 16-row tile) and weight
+//    columns as N: warp w owns columns 16w .. 16w+15.
+//  * From 17 tokens on, Kernel D2 (tcgen05, K split over the SMs) is faster
+//    at every config-3 shape: a second 16-row tile doubles this kernel's
+//    activation footprint and halves its CTAs per SM (at 32 tokens gate/up
+//    73.6 us and down 64.5 us here against 58.2 us and 30.6 us there).
 //  * Dequantisation as the reference (nanovllm/layers/linear_w4a16.py:45-55):
 //    bf16(128 + w) - bf16(129 + z) = w - z - 1 exactly, times the BF16-rounded
 //    FP16 scale with one BF16 rounding (BF16x2 subtract and multiply).
@@ -486,11 +490,13 @@ __global__ void __launch_bounds__(128) w4a16_stream_kernel(const __grid_constant
 // K slice is at most 1024 (its weights and activations then fit several CTAs
 // per SM, so one CTA's loads overlap another's math).
 struct W4A16StreamPlan {
-  int ks, k_slice, mtiles, x_stride, smem;
+  int ks, k_slice, x_stride, smem;
 };
 
+constexpr int64_t kW4A16StreamMaxM = 16;  // tokens Kernel D1 takes (one MMA tile)
+
 static bool plan_w4a16_stream(int64_t m, int64_t n, int64_t k, int sms, W4A16StreamPlan* out) {
-  if (m > 32 || n % kW4A16StreamCols || k % 256) return false;
+  if (m > kW4A16StreamMaxM || n % kW4A16StreamCols || k % 256) return false;
   const int64_t tiles = n / kW4A16StreamCols;
   int ks = 1;
   while (ks < 8 && (tiles * ks < 3 * static_cast<int64_t>(sms) || k / ks > 1024) && (k / (2 * ks)) % 256 == 0)
@@ -499,9 +505,8 @@ static bool plan_w4a16_stream(int64_t m, int64_t n, int64_t k, int sms, W4A16Str
   pl.ks = ks;
   pl.k_slice = static_cast<int>(k / ks);
   if (pl.k_slice / 256 > kW4A16MaxChunks) return false;
-  pl.mtiles = m <= 16 ? 1 : 2;
   pl.x_stride = pl.k_slice * 2 + 16;  // 16 bytes of padding: conflict-free ldmatrix rows
-  const W4A16StreamLayout L(pl.k_slice, static_cast<int>(std::min<int64_t>(m, 16 * pl.mtiles)), pl.x_stride);
+  const W4A16StreamLayout L(pl.k_slice, static_cast<int>(m), pl.x_stride);
   pl.smem = L.total;
   if (pl.smem > 227 * 1024) return false;
   *out = pl;
@@ -557,8 +562,7 @@ static int launch_w4a16_stream(const void* x, const void* qweight, const void* q
   a.k_slice = pl.k_slice;
   a.chunks = pl.k_slice / 256;
   a.x_stride = pl.x_stride;
-  return pl.mtiles == 1 ? launch_w4a16_stream_t<1>(map, a, pl, n, stream)
-                        : launch_w4a16_stream_t<2>(map, a, pl, n, stream);
+  return launch_w4a16_stream_t<1>(map, a, pl, n, stream);
 }
 
 int64_t w4a16_workspace_bytes(int64_t m, int64_t n, int64_t k) {
@@ -566,11 +570,12 @@ int64_t w4a16_workspace_bytes(int64_t m, int64_t n, int64_t k) {
   if (sms <= 0) return 0;
   W4A16StreamPlan sp;
   if (plan_w4a16_stream(m, n, k, sms, &sp)) return 0;
-  if (m > 32) return std::max(w4a16_tc_workspace_bytes(m, n, k), w4a16_mma_workspace_bytes(m, n, k, sms));
+  if (m > kW4A16StreamMaxM)
+    return std::max(w4a16_tc_workspace_bytes(m, n, k), w4a16_mma_workspace_bytes(m, n, k, sms));
   return w4a16_mma_workspace_bytes(m, n, k, sms);
 }
 
-// Up to 32 tokens: Kernel D1 (no workspace); more: Kernel D2 (tcgen05, split-K
+// Up to 16 tokens: Kernel D1 (no workspace); more: Kernel D2 (tcgen05, split-K
 // partials in the workspace when its plan splits); shapes neither takes: the
 // mma.sync kernel.
 int launch_w4a16_gemm(const void* x, const void* qweight, const void* qzeros, const void* scales, void* out,
@@ -580,7 +585,7 @@ int launch_w4a16_gemm(const void* x, const void* qweight, const void* qzeros, co
   W4A16StreamPlan sp;
   if (plan_w4a16_stream(m, n, k, sms, &sp) && (reinterpret_cast<uintptr_t>(qweight) & 15) == 0)
     return launch_w4a16_stream(x, qweight, qzeros, scales, out, m, n, k, sp, stream);
-  if (m > 32) {
+  if (m > kW4A16StreamMaxM) {
     const int rc = launch_w4a16_tc_gemm(x, qweight, qzeros, scales, out, m, n, k, workspace, workspace_bytes, stream);
     if (rc != NV4_ERR_UNSUPPORTED) return rc;
   }

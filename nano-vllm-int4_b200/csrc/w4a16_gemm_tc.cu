@@ -1,5 +1,5 @@
 // Kernel D2: GPTQ W4A16 dequant GEMM on 5th-generation tensor cores (tcgen05
-// kind::f16), for prefill-shape token counts (more than 32 tokens).
+// kind::f16), for more than 16 tokens.
 //
 // out[m, n] = sum_k x[m, k] * Wdq[k, n] with the reference's dequantisation
 // (nanovllm/layers/linear_w4a16.py:45-55): Wdq = bf16((w - z - 1) * bf16(scale)),

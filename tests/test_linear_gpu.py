@@ -114,7 +114,7 @@ def test_tp_shards_single_gpu(cuda_device, tp):
 
 
 @pytest.mark.parametrize("n,k", [(6144, 4096), (24576, 4096), (4096, 12288)])
-@pytest.mark.parametrize("m", [1, 16, 128])
+@pytest.mark.parametrize("m", [1, 16, 17, 32, 128])
 def test_w4a16_matches_oracle(cuda_device, n, k, m):
     qweight, qzeros, scales = synthetic.w4a16_weights(n, k, seed=n + k)
     layer = W4A16Linear(k, n).to(cuda_device)
@@ -136,7 +136,7 @@ def test_w4a16_matches_oracle(cuda_device, n, k, m):
 @pytest.mark.parametrize("m,n,k", [(33, 192, 512), (300, 320, 1024), (257, 4096, 12288), (2048, 24576, 4096),
                                    (128, 6144, 4096), (128, 4096, 12288)])
 def test_w4a16_prefill_tiles(cuda_device, m, n, k):
-    """The tcgen05 W4A16 kernel (more than 32 tokens): ragged token and column
+    """The tcgen05 W4A16 kernel (more than 16 tokens): ragged token and column
     tiles (zero-filled TMA boxes past M and N, stores masked), K split into 2-8
     slices (uneven ones at 128 x 6144 x 4096) summed by the second kernel, and
     an unsplit full config-3 prefill shape, on a sample of rows against the

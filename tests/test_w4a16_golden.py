@@ -6,7 +6,7 @@ statement-by-statement torch restatement of the reference's TileLang kernel
   and so does its exact product rounded to BF16.
 * GPU: the dequantised weights (read back through one-hot activation rows, for
   which every output element is a single weight times one) equal the
-  reference's bit for bit on both kernels (decode: up to 32 tokens; prefill);
+  reference's bit for bit on both kernels (decode: up to 16 tokens; tcgen05);
   GEMM outputs agree with the reference's exact BF16 product within rel-L2 1e-3,
   the north-star tolerance, and bit for bit on at least 99% of the elements.
 """
@@ -72,11 +72,12 @@ def _layer(qweight, qzeros, scales, device):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("rows", [32, 256])
+@pytest.mark.parametrize("rows", [16, 32, 256])
 def test_dequantized_weights_bit_exact(cuda_device, rows):
     """One-hot activation rows: out[r, :] = W[r, :] exactly (a single nonzero
-    product, FP32 sum, BF16 rounding of a BF16 value).  32-row slices run the
-    decode kernel, the full identity the prefill kernel."""
+    product, FP32 sum, BF16 rounding of a BF16 value).  16-row slices run the
+    decode kernel; 32-row slices and the full identity the tcgen05 kernel, with
+    K split (the other slices add exact zeros)."""
     name, n, k = gen.IDENTITY
     eye, qweight, qzeros, scales = gen.identity_inputs(n, k)
     layer = _layer(qweight, qzeros, scales, cuda_device)
