@@ -147,7 +147,7 @@ int nv4_w4a4_group_dots(const void* a_packed, const void* w_packed, int32_t* dot
  *   scales   fp16 [k/group_size, n]
  *   out      bf16 [m, n]
  *   workspace   float32 scratch of nv4_w4a16_workspace_bytes(m, n, k) bytes
- *               (may be NULL when that size is 0).  Above 32 tokens it holds
+ *               (may be NULL when that size is 0).  Above 16 tokens it holds
  *               the FP32 partials of a K split (16-byte aligned, `out` 8-byte
  *               aligned); NULL or smaller there runs the GEMM unsplit.
  * Requirements: group_size == 128, k % 128 == 0, n % 64 == 0.
