@@ -158,6 +158,24 @@ int nv4_w4a16_gemm(const void* x, const void* qweight, const void* qzeros, const
 int64_t nv4_w4a16_workspace_bytes(int64_t m, int64_t n, int64_t k);
 
 /*
+ * Which kernel nv4_w4a16_gemm runs for a shape, and its split, computed on the
+ * host only (no GPU or CUDA call; sm_count is 148 on B200), assuming 16-byte
+ * aligned operands and a workspace of nv4_w4a16_workspace_bytes.  No reference
+ * counterpart: the reference launches one fixed configuration (BLOCK_M 16,
+ * BLOCK_N 64, BLOCK_K 32, SPLIT_K 8; nanovllm/layers/linear_w4a16.py:138-146).
+ * plan receives NV4_W4A16_PLAN_FIELDS int64 values, in order: kernel
+ * (NV4_W4A16_KERNEL_*), K splits (cluster CTAs along K for the decode kernel,
+ * K slices for the tcgen05 kernel, 1 = none), token tile, CTAs, workspace
+ * bytes.  Returns NV4_OK, or NV4_ERR_INVALID_ARGUMENT for a shape or
+ * sm_count nv4_w4a16_gemm would reject.
+ */
+#define NV4_W4A16_PLAN_FIELDS 5
+#define NV4_W4A16_KERNEL_MMA 0    /* mma.sync tiles (shapes the others do not take) */
+#define NV4_W4A16_KERNEL_DECODE 1 /* up to 16 tokens: TMA weight stream, cluster split-K */
+#define NV4_W4A16_KERNEL_TC 2     /* more than 16 tokens: tcgen05, K split when tiles do not fill the SMs */
+int nv4_w4a16_plan(int64_t m, int64_t n, int64_t k, int sm_count, int64_t* plan);
+
+/*
  * nv4_w4a16_gemm without a workspace argument (no counterpart in the
  * reference, whose kernel adds into a pre-zeroed output instead).  Same
  * arguments, requirements and results as nv4_w4a16_gemm.

@@ -290,6 +290,15 @@ int nv4_w4a16_gemm(const void* x, const void* qweight, const void* qzeros, const
                            static_cast<cudaStream_t>(stream));
 }
 
+int nv4_w4a16_plan(int64_t m, int64_t n, int64_t k, int sm_count, int64_t* plan) {
+  if (plan == nullptr || sm_count < 1) return NV4_ERR_INVALID_ARGUMENT;
+  if (m < 1 || n < 64 || k < 128 || k % 128 || n % 64 || m > (int64_t(1) << 31) - 1 || k > (int64_t(1) << 24) ||
+      n > (int64_t(1) << 24))
+    return NV4_ERR_INVALID_ARGUMENT;
+  w4a16_plan(m, n, k, sm_count, plan);
+  return NV4_OK;
+}
+
 // Allocation-free variant: the split-K partials go to a static device array
 // (see launch_w4a16_gemm_static).  Checks as nv4_w4a16_gemm, plus the
 // scratch limit.

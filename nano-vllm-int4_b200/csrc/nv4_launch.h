@@ -80,6 +80,8 @@ int launch_w4a16_tc_gemm(const void* x, const void* qweight, const void* qzeros,
                          int64_t m, int64_t n, int64_t k, void* workspace, int64_t workspace_bytes,
                          cudaStream_t stream);
 int64_t w4a16_tc_workspace_bytes(int64_t m, int64_t n, int64_t k);
+bool w4a16_tc_plan(int64_t m, int64_t n, int64_t k, int sms, int* bn, int* splits);
+void w4a16_plan(int64_t m, int64_t n, int64_t k, int sms, int64_t* plan);  // NV4_W4A16_PLAN_FIELDS values
 // Same as launch_w4a16_gemm with the library's static scratch as workspace.
 int launch_w4a16_gemm_static(const void* x, const void* qweight, const void* qzeros, const void* scales, void* out,
                              int64_t m, int64_t n, int64_t k, cudaStream_t stream);

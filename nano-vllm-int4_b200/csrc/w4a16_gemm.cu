@@ -575,6 +575,29 @@ int64_t w4a16_workspace_bytes(int64_t m, int64_t n, int64_t k) {
   return w4a16_mma_workspace_bytes(m, n, k, sms);
 }
 
+// The dispatch of launch_w4a16_gemm below for 16-byte aligned operands and a
+// workspace of w4a16_workspace_bytes, on `sms` SMs, as plain numbers: kernel
+// (1 decode stream, 2 tcgen05, 0 mma.sync), K splits, token tile, CTAs,
+// workspace bytes.
+void w4a16_plan(int64_t m, int64_t n, int64_t k, int sms, int64_t* plan) {
+  W4A16StreamPlan sp;
+  int bn = 0, splits = 1;
+  if (plan_w4a16_stream(m, n, k, sms, &sp)) {
+    const int64_t v[5] = {1, sp.ks, 16, (n / kW4A16StreamCols) * sp.ks, 0};
+    for (int i = 0; i < 5; ++i) plan[i] = v[i];
+  } else if (m > kW4A16StreamMaxM && w4a16_tc_plan(m, n, k, sms, &bn, &splits)) {
+    const int64_t units = ((n + 127) / 128) * ((m + bn - 1) / bn) * splits;
+    const int64_t v[5] = {2, splits, bn, std::min<int64_t>(units, sms),
+                          splits > 1 ? splits * m * n * static_cast<int64_t>(sizeof(float)) : 0};
+    for (int i = 0; i < 5; ++i) plan[i] = v[i];
+  } else {
+    const W4A16Plan pl = plan_w4a16(m, n, k, sms);
+    const int64_t v[5] = {0, pl.splits, pl.bm, ((n + pl.bn - 1) / pl.bn) * ((m + pl.bm - 1) / pl.bm) * pl.splits,
+                          pl.splits > 1 ? m * n * static_cast<int64_t>(sizeof(float)) : 0};
+    for (int i = 0; i < 5; ++i) plan[i] = v[i];
+  }
+}
+
 // Up to 16 tokens: Kernel D1 (no workspace); more: Kernel D2 (tcgen05, split-K
 // partials in the workspace when its plan splits); shapes neither takes: the
 // mma.sync kernel.

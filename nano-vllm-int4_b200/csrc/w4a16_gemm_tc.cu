@@ -461,12 +461,22 @@ static D2Plan plan_w4a16_tc(int64_t m, int64_t n, int64_t k, int sms) {
   return pl;
 }
 
+// The shape rules of this kernel (pointer alignment aside) and its plan.
+bool w4a16_tc_plan(int64_t m, int64_t n, int64_t k, int sms, int* bn, int* splits) {
+  if (m < 1 || n < 32 || n % 32 || k < 128 || k % 128 || m > (int64_t(1) << 30) || n > (int64_t(1) << 30) ||
+      sms < 1)
+    return false;
+  const D2Plan pl = plan_w4a16_tc(m, n, k, sms);
+  *bn = pl.bn;
+  *splits = pl.splits;
+  return true;
+}
+
 // Workspace the split plan of a shape wants (0: no split).
 int64_t w4a16_tc_workspace_bytes(int64_t m, int64_t n, int64_t k) {
-  const int sms = device_sm_count();
-  if (sms <= 0 || m < 1 || n < 32 || k < 128) return 0;
-  const D2Plan pl = plan_w4a16_tc(m, n, k, sms);
-  return pl.splits > 1 ? pl.splits * m * n * static_cast<int64_t>(sizeof(float)) : 0;
+  int bn = 0, splits = 1;
+  if (!w4a16_tc_plan(m, n, k, device_sm_count(), &bn, &splits)) return 0;
+  return splits > 1 ? splits * m * n * static_cast<int64_t>(sizeof(float)) : 0;
 }
 
 // Shapes outside the kernel's alignment rules return NV4_ERR_UNSUPPORTED (the
@@ -476,13 +486,13 @@ int64_t w4a16_tc_workspace_bytes(int64_t m, int64_t n, int64_t k) {
 int launch_w4a16_tc_gemm(const void* x, const void* qweight, const void* qzeros, const void* scales, void* out,
                          int64_t m, int64_t n, int64_t k, void* workspace, int64_t workspace_bytes,
                          cudaStream_t stream) {
-  if (m < 1 || n < 32 || n % 32 || k < 128 || k % 128 || (reinterpret_cast<uintptr_t>(x) & 15) ||
-      (reinterpret_cast<uintptr_t>(qweight) & 15) || (reinterpret_cast<uintptr_t>(qzeros) & 15) ||
-      (reinterpret_cast<uintptr_t>(scales) & 15) || m > (int64_t(1) << 30) || n > (int64_t(1) << 30))
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(qweight) & 15) ||
+      (reinterpret_cast<uintptr_t>(qzeros) & 15) || (reinterpret_cast<uintptr_t>(scales) & 15))
     return NV4_ERR_UNSUPPORTED;
   const int sms = device_sm_count();
   if (sms <= 0) return NV4_ERR_CUDA;
-  D2Plan pl = plan_w4a16_tc(m, n, k, sms);
+  D2Plan pl;
+  if (!w4a16_tc_plan(m, n, k, sms, &pl.bn, &pl.splits)) return NV4_ERR_UNSUPPORTED;
   if (pl.splits > 1 && (workspace == nullptr || workspace_bytes < pl.splits * m * n * static_cast<int64_t>(sizeof(float)) ||
                         (reinterpret_cast<uintptr_t>(workspace) & 15) || (reinterpret_cast<uintptr_t>(out) & 7)))
     pl.splits = 1;

@@ -38,7 +38,7 @@ EXPORTS = ("nv4_rht_quant_pack", "nv4_rht_quant_i8", "nv4_w4a4_grouped_gemm", "n
            "nv4_peer_buffer_open", "nv4_peer_buffer_close", "nv4_peer_buffer_free", "nv4_peer_allreduce_bf16",
            "nv4_w4a4_gemm_peer_allreduce_bf16", "nv4_silu_mul_rht_quant_i8",
            "nv4_add_rmsnorm_rht_quant_i8", "nv4_w4a4_stream_plan", "nv4_paged_attention_workspace_bytes",
-           "nv4_paged_decode_attention", "nv4_qk_norm_rope_store")
+           "nv4_paged_decode_attention", "nv4_qk_norm_rope_store", "nv4_w4a16_plan")
 
 
 class NativeLibraryError(RuntimeError):
@@ -122,6 +122,8 @@ def load(path: str | None = None) -> ctypes.CDLL:
         lib.nv4_w4a16_workspace_bytes.restype = _i64
         lib.nv4_w4a4_stream_plan.argtypes = [_i64, _i64, _i64, _int, _int, _int, ctypes.POINTER(ctypes.c_int32)]
         lib.nv4_w4a4_stream_plan.restype = _int
+        lib.nv4_w4a16_plan.argtypes = [_i64, _i64, _i64, _int, ctypes.POINTER(ctypes.c_int64)]
+        lib.nv4_w4a16_plan.restype = _int
         lib.nv4_paged_attention_workspace_bytes.argtypes = [_i64, _i64, _i64]
         lib.nv4_paged_attention_workspace_bytes.restype = _i64
         lib.nv4_paged_decode_attention.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
@@ -274,6 +276,18 @@ def w4a4_stream_plan(m: int, n: int, k: int, flags: int = GEMM_W_SCALE_GROUPED, 
         return None
     check(status, "nv4_w4a4_stream_plan")
     return dict(zip(STREAM_PLAN_FIELDS, list(out)))
+
+
+W4A16_PLAN_FIELDS = ("kernel", "splits", "token_tile", "ctas", "workspace_bytes")
+W4A16_KERNEL_MMA, W4A16_KERNEL_DECODE, W4A16_KERNEL_TC = 0, 1, 2
+
+
+def w4a16_plan(m: int, n: int, k: int, sm_count: int = SM_COUNT_B200):
+    """Which W4A16 kernel nv4_w4a16_gemm runs for a shape and its K split
+    (nv4_w4a16_plan; host only, no GPU needed): a dict of W4A16_PLAN_FIELDS."""
+    out = (ctypes.c_int64 * len(W4A16_PLAN_FIELDS))()
+    check(load().nv4_w4a16_plan(m, n, k, sm_count, out), "nv4_w4a16_plan")
+    return dict(zip(W4A16_PLAN_FIELDS, list(out)))
 
 
 # ---------------------------------------------------------------- tensor-parallel peer buffers
