@@ -440,6 +440,7 @@ def measure_w4a16(device, stream, peaks):
     """Config 3: W4A16Linear at M in {1, 16, 128, 2048}, plus 32 (the decode
     batch of the end-to-end model).  Small M streams
     distinct weight copies (more than 256 MB in total, larger than L2)."""
+    from nanovllm import _native
     from nanovllm.layers.linear_w4a16 import W4A16Linear
     out = {}
     shapes = [("qkv", 6144, 4096), ("gate_up", 24576, 4096), ("down", 4096, 12288)]
@@ -467,6 +468,9 @@ def measure_w4a16(device, stream, peaks):
                     lin(x)
             t = time_launches(calls, len(use), stream, 10 if m <= 128 else 3)
             r = {"us": t * 1e6, "gbs": w4a16_bytes(m, n, k) / t / 1e9, "tflops": 2 * m * n * k / t / 1e12}
+            pl = _native.w4a16_plan(m, n, k, torch.cuda.get_device_properties(device).multi_processor_count)
+            r["kernel"] = {0: "mma.sync", 1: "decode stream", 2: "tcgen05"}[pl["kernel"]]
+            r["k_splits"] = pl["splits"]
             r["frac_hbm"] = r["gbs"] / peaks["hbm_gbs"]
             r["frac_bf16"] = r["tflops"] / peaks["bf16_tflops"]
             r["frac_bf16_sustained"] = r["tflops"] / peaks["bf16_tflops_sustained"]
